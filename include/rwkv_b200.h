@@ -1,0 +1,153 @@
+/*
+ * rwkv_b200.h -- C ABI of the B200 (sm_100a) RWKV-7 forward hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream, allocates no
+ * device memory itself (scratch comes from a caller-provided workspace), and
+ * returns 0 on success or a nonzero RWKV_ERR_* code; the message is available
+ * from rwkv_b200_last_error() (thread-local). There is no CPU fallback.
+ *
+ * Tensor conventions: fp16 activations and weights ("half" = IEEE binary16,
+ * passed as void*), fp32 wkv state, row-major. Weight matrices keep the
+ * checkpoint's [out, in] orientation so both the GEMV (decode) and the
+ * K-major tensor-core GEMM (prefill) read them contiguously along `in`.
+ *
+ * Reference interfaces replaced (yuyi2439/rwkv-tl, paths within that project):
+ *   rwkv7_dplr_step     <- Kernels.fused_dplr      src/rwkv_tl/kernels/dplr.py:256-270
+ *                          (torch.ops.rwkv_tl.fused_dplr, src/rwkv_tl/operators/__init__.py:315-322)
+ *   rwkv7_dplr_seq      <- Kernels.fused_dplr_T    src/rwkv_tl/kernels/dplr.py:272-285
+ *   rwkv7_gemm_f16      <- Kernels.fused_rkv_gemm / ffn_h / ffn_v / out_mm
+ *                          src/rwkv_tl/kernels/gemm.py:215-305
+ *   rwkv7_forward       <- RWKV7Base.prefill / RWKV7Base.decode layer loops
+ *                          demo/_rwkv7_base.py:74-98 (TMIX :153-206 / :223-272,
+ *                          CMIX :285-290 / :300-308), batched over sequences
+ *   rwkv7_decode_gemv   <- RWKV7Base.decode (demo/_rwkv7_base.py:74-87) for
+ *                          small batches, the CUDA-Graph decode body of
+ *                          demo/cuda_graph.py:111-128
+ */
+#ifndef RWKV_B200_H_
+#define RWKV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RWKV_B200_ABI_VERSION 1
+
+enum {
+  RWKV_OK = 0,
+  RWKV_ERR_ARG = 1,     /* bad shape / null pointer / unsupported size */
+  RWKV_ERR_CUDA = 2,    /* a CUDA launch or runtime call failed */
+  RWKV_ERR_SPACE = 3    /* workspace too small */
+};
+
+/* Rounding semantics. The reference's fp16 decode path rounds to fp16 only at
+ * its fused-kernel stores (src/rwkv_tl/kernels/{lerp,gates,dplr}.py); its
+ * prefill path rounds after every torch op (demo/_rwkv7_base.py:223-310).
+ * RWKV_SEM_DECODE reproduces the former, RWKV_SEM_PREFILL the latter. */
+enum { RWKV_SEM_DECODE = 0, RWKV_SEM_PREFILL = 1 };
+
+/* GEMM epilogues: C = f(A @ B^T) with fp32 accumulation. */
+enum {
+  RWKV_EPI_STORE = 0,  /* C = fp16(acc)                                  */
+  RWKV_EPI_RESID = 1,  /* C = fp16(R + fp16(acc))          (x0 + y @ W)  */
+  RWKV_EPI_RELUSQ = 2  /* C = fp16(relu(fp16(acc))^2)      (FFN key)     */
+};
+
+/* Per-layer weights (device pointers, fp16). C = n_embd, H = C/64. */
+typedef struct rwkv7_layer {
+  const void* ln1_w; const void* ln1_b;   /* [C]                                 */
+  const void* ln2_w; const void* ln2_b;   /* [C]                                 */
+  const void* mix6;       /* [6, C]  x_r, x_w, x_k, x_v, x_a, x_g                  */
+  const void* w_rkv;      /* [3C, C] receptance | key | value weights ([out, in])  */
+  const void* w_lora_dn;  /* [288, C] v1^T(32) | w1^T(64) | a1^T(64) | g1^T(128)   */
+  const void* w_lora_up;  /* [288, C] v2(32) | w2(64) | a2(64) | g2(128)  ([r, C]) */
+  const void* w0; const void* a0; const void* v0;   /* [C] gate biases           */
+  const void* k_k; const void* k_a;       /* [C]                                 */
+  const void* r_k;        /* [C] (= [H, 64])                                       */
+  const void* lnx_w; const void* lnx_b;   /* [C] per-head GroupNorm affine       */
+  const void* w_o;        /* [C, C] output projection ([out, in])                  */
+  const void* ffn_x_k;    /* [C]                                                   */
+  const void* w_fk;       /* [4C, C] FFN key                                       */
+  const void* w_fv;       /* [C, 4C] FFN value                                     */
+} rwkv7_layer;
+
+typedef struct rwkv7_model {
+  int n_layer, n_embd, vocab;
+  int rank_v, rank_w, rank_a, rank_g;     /* must be 32, 64, 64, 128          */
+  const void* emb;        /* [V, C] embedding with LN0 already applied           */
+  const void* head;       /* [V, C]                                              */
+  const void* lnout_w; const void* lnout_b; /* [C]                               */
+  const rwkv7_layer* layers;  /* HOST array of n_layer entries                  */
+} rwkv7_model;
+
+/* Recurrent state of `n_slots` sequences, one contiguous block per tensor:
+ *   rnn    fp32 [L, n_slots, H, 64, 64]   (row = value index, column = key index,
+ *                                          the layout of State.tmix[i]["rnn"])
+ *   tmix_x fp16 [L, n_slots, C]           (State.tmix[i]["x"])
+ *   cmix_x fp16 [L, n_slots, C]           (State.cmix[i]["x"])
+ * (src/rwkv_tl/state.py:31-44, with a leading layer and slot dimension). */
+typedef struct rwkv7_state {
+  void* rnn; void* tmix_x; void* cmix_x;
+  int n_slots;
+} rwkv7_state;
+
+/* A batch of token rows. Rows of sequence s are [cu_seqlens[s], cu_seqlens[s+1]),
+ * consecutive in time; sequence s uses state slot slots[s] (NULL: slot s).
+ * All arrays are device pointers. */
+typedef struct rwkv7_batch {
+  int n_rows, n_seqs;
+  const int64_t* tokens;    /* [n_rows]                                         */
+  const int* cu_seqlens;    /* [n_seqs + 1]                                     */
+  const int* row_seq;       /* [n_rows] sequence index of each row              */
+  const int* slots;         /* [n_seqs] or NULL                                 */
+  int n_logits;             /* rows that produce logits (0: state update only)  */
+  const int* logit_rows;    /* [n_logits] row indices                           */
+  void* logits;             /* fp16 [n_logits, V]                               */
+  int semantics;            /* RWKV_SEM_DECODE or RWKV_SEM_PREFILL              */
+} rwkv7_batch;
+
+const char* rwkv_b200_last_error(void);
+int rwkv_b200_abi_version(void);
+
+/* wkv7 DPLR step, batched over n_seq independent sequences (T = 1):
+ *   sa[v] = sum_j S[v,j] a[j];  S[v,k] = S[v,k] w[k] + sa[v] b[k] + v[v] k[k];
+ *   y[v]  = sum_k S[v,k] r[k]      (S updated in place, y stored fp16)
+ * S: fp32 [n_seq, H, 64, 64]; r, w, k, v, a, b, y: fp16 [n_seq, H, 64].
+ * Argument order follows fused_dplr(S, R, W, K, V, A, B). */
+int rwkv7_dplr_step(void* S, const void* r, const void* w, const void* k, const void* v,
+                    const void* a, const void* b, void* y, int n_seq, int H, void* stream);
+
+/* The same recurrence over T consecutive tokens of one sequence (fused_dplr_T):
+ * r..b, y: fp16 [T, H, 64]; S: fp32 [H, 64, 64] updated in place. */
+int rwkv7_dplr_seq(void* S, const void* r, const void* w, const void* k, const void* v,
+                   const void* a, const void* b, void* y, int T, int H, void* stream);
+
+/* Grouped fp16 GEMM, up to 4 independent problems in one launch:
+ *   C_g[M_g, N_g] = epi( A_g[M_g, K_g] @ B_g[N_g, K_g]^T )
+ * A row-major (lda), B row-major [N, K] (ldb), C/R row-major (ldc). K_g must be
+ * a multiple of 32, lda/ldb/ldc multiples of 8; M and N arbitrary. */
+typedef struct rwkv7_gemm_problem {
+  const void* A; const void* B; void* C; const void* R;
+  int M, N, K, lda, ldb, ldc;
+} rwkv7_gemm_problem;
+int rwkv7_gemm_f16(const rwkv7_gemm_problem* problems, int n_problems, int epilogue,
+                   void* stream);
+
+/* Full forward of a token batch through all layers (prefill of any number of
+ * sequences, or one decode step of many sequences), updating `state` in place
+ * and writing logits for batch->logit_rows. Needs a device workspace of at
+ * least rwkv7_forward_workspace_bytes(...) bytes (256-byte aligned). */
+size_t rwkv7_forward_workspace_bytes(const rwkv7_model* model, int n_rows, int n_seqs,
+                                     int n_logits);
+int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* batch,
+                  const rwkv7_state* state, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RWKV_B200_H_ */

@@ -1,0 +1,234 @@
+// C-ABI entry points: error reporting and the token-batch forward driver.
+//
+// rwkv7_forward runs the layer loop of RWKV7Base.prefill / decode
+// (demo/_rwkv7_base.py:74-98) for a batch of token rows of many sequences:
+// per layer TMIX (row LN+shift+mix -> r/k/v GEMM -> LoRA-down GEMM -> gates ->
+// wkv+GroupNorm+gate -> output GEMM + residual) and CMIX (row LN+shift+mix ->
+// key GEMM + relu^2 -> value GEMM + residual), then ln_out + head GEMM for the
+// requested rows and the state-x write-back.
+#include <cstdarg>
+#include <cstdio>
+
+#include "common.cuh"
+
+static thread_local char g_err[512] = "";
+
+void rwkv_set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int rwkv_check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    rwkv_set_error("%s: CUDA error %s", what, cudaGetErrorString(e));
+    return RWKV_ERR_CUDA;
+  }
+  return RWKV_OK;
+}
+
+extern "C" const char* rwkv_b200_last_error(void) { return g_err; }
+extern "C" int rwkv_b200_abi_version(void) { return RWKV_B200_ABI_VERSION; }
+
+// launchers from the other translation units
+int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* emb,
+                     const __half* ln_w, const __half* ln_b, const __half* mix6,
+                     const __half* state_x, const int* row_seq, const int* cu, const int* slots,
+                     __half* xmix, __half* xlast, int M, int C, cudaStream_t st);
+int launch_cmix_rows(int sem, const __half* x, const __half* ln_w, const __half* ln_b,
+                     const __half* mu, const __half* state_x, const int* row_seq, const int* cu,
+                     const int* slots, __half* xk, __half* xlast, int M, int C, cudaStream_t st);
+int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __half* b,
+                   __half* out, int n, int C, cudaStream_t st);
+int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,
+                           int S, int L, int n_slots, int C, cudaStream_t st);
+int launch_gates(int sem, const __half* ranks, const __half* w_up, const __half* rkv,
+                 const __half* w0, const __half* a0, const __half* v0, const __half* k_k,
+                 const __half* k_a, __half* vfirst, __half* gout, int M, int C, int layer0,
+                 cudaStream_t st);
+int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t plane,
+                      const __half* r_k, const __half* lnx_w, const __half* lnx_b, float* rnn,
+                      const int* cu, const int* slots, __half* yg, int n_seqs, int H, int C,
+                      cudaStream_t st);
+int gemm_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStream_t st);
+
+namespace {
+
+struct Carve {
+  char* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    T* p = reinterpret_cast<T*>(base ? base + off : nullptr);
+    off += (count * sizeof(T) + 255) & ~size_t(255);
+    return p;
+  }
+};
+
+struct Work {
+  __half *x, *x1, *xmix, *rkv, *ranks, *gbuf, *vfirst, *yg, *xk, *h, *xlast, *lnout;
+};
+
+Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) {
+  Carve c(base);
+  const size_t MC = (size_t)M * C;
+  Work w;
+  w.x = c.take<__half>(MC);
+  w.x1 = c.take<__half>(MC);
+  w.xmix = c.take<__half>(6 * MC);
+  w.rkv = c.take<__half>(3 * MC);
+  w.ranks = c.take<__half>((size_t)M * RWKV_RANK_SUM);
+  w.gbuf = c.take<__half>(6 * MC);
+  w.vfirst = c.take<__half>(MC);
+  w.yg = c.take<__half>(MC);
+  w.xk = c.take<__half>(MC);
+  w.h = c.take<__half>(4 * MC);
+  w.xlast = c.take<__half>((size_t)L * 2 * S * C);
+  w.lnout = c.take<__half>((size_t)n_logits * C);
+  total = c.off;
+  return w;
+}
+
+int check_model(const rwkv7_model* m) {
+  if (!m || !m->layers || !m->emb || !m->head || m->n_layer <= 0) {
+    rwkv_set_error("rwkv7_model: null pointer or no layers");
+    return RWKV_ERR_ARG;
+  }
+  if (m->n_embd % 128 || m->n_embd < 128 || m->n_embd > 4096) {
+    rwkv_set_error("rwkv7_model: n_embd must be a multiple of 128 in [128, 4096] (got %d)",
+                   m->n_embd);
+    return RWKV_ERR_ARG;
+  }
+  if (m->rank_v != RWKV_RANK_V || m->rank_w != RWKV_RANK_W || m->rank_a != RWKV_RANK_A ||
+      m->rank_g != RWKV_RANK_G) {
+    rwkv_set_error("rwkv7_model: LoRA ranks must be v=32 w=64 a=64 g=128 (got %d %d %d %d)",
+                   m->rank_v, m->rank_w, m->rank_a, m->rank_g);
+    return RWKV_ERR_ARG;
+  }
+  if (m->vocab <= 0 || m->vocab % 2) {
+    rwkv_set_error("rwkv7_model: vocab must be positive and even (got %d)", m->vocab);
+    return RWKV_ERR_ARG;
+  }
+  return RWKV_OK;
+}
+
+#define TRY(expr)         \
+  do {                    \
+    int _rc = (expr);     \
+    if (_rc) return _rc;  \
+  } while (0)
+
+}  // namespace
+
+extern "C" size_t rwkv7_forward_workspace_bytes(const rwkv7_model* model, int n_rows, int n_seqs,
+                                                int n_logits) {
+  if (check_model(model) || n_rows < 0 || n_seqs < 0 || n_logits < 0) return 0;
+  size_t total = 0;
+  carve(nullptr, total, n_rows, n_seqs, model->n_layer, model->n_embd, n_logits);
+  return total;
+}
+
+extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
+                             const rwkv7_state* state, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  TRY(check_model(model));
+  if (!b || !state || !state->rnn || !state->tmix_x || !state->cmix_x) {
+    rwkv_set_error("rwkv7_forward: null batch/state");
+    return RWKV_ERR_ARG;
+  }
+  const int M = b->n_rows, S = b->n_seqs, L = model->n_layer, C = model->n_embd, H = C / RWKV_HD;
+  if (M <= 0 || S <= 0 || S > M || !b->tokens || !b->cu_seqlens || !b->row_seq ||
+      b->n_logits < 0 || (b->n_logits && (!b->logit_rows || !b->logits)) ||
+      (b->semantics != RWKV_SEM_DECODE && b->semantics != RWKV_SEM_PREFILL) ||
+      (!b->slots && S > state->n_slots)) {
+    rwkv_set_error("rwkv7_forward: bad batch (rows=%d seqs=%d logits=%d semantics=%d)", M, S,
+                   b->n_logits, b->semantics);
+    return RWKV_ERR_ARG;
+  }
+  if ((size_t)M * 4 * C > ((size_t)1 << 31)) {
+    rwkv_set_error("rwkv7_forward: too many rows in one call (%d); split the batch", M);
+    return RWKV_ERR_ARG;
+  }
+  size_t need = 0;
+  Work w = carve(workspace, need, M, S, L, C, b->n_logits);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) {
+    rwkv_set_error("rwkv7_forward: workspace needs %zu bytes, 256-aligned (got %zu)", need,
+                   workspace_bytes);
+    return RWKV_ERR_SPACE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const int sem = b->semantics;
+  const size_t MC = (size_t)M * C;
+  const size_t CC = (size_t)C * C;
+  const int ns = state->n_slots;
+  const __half* emb = (const __half*)model->emb;
+
+  for (int l = 0; l < L; ++l) {
+    const rwkv7_layer& Lw = model->layers[l];
+    const __half* wrkv = (const __half*)Lw.w_rkv;
+    const __half* wdn = (const __half*)Lw.w_lora_dn;
+    __half* st_tx = (__half*)state->tmix_x + (size_t)l * ns * C;
+    __half* st_cx = (__half*)state->cmix_x + (size_t)l * ns * C;
+    float* st_rnn = (float*)state->rnn + (size_t)l * ns * H * RWKV_HD * RWKV_HD;
+    __half* xl_t = w.xlast + ((size_t)l * 2 + 0) * S * C;
+    __half* xl_c = w.xlast + ((size_t)l * 2 + 1) * S * C;
+
+    // ---- TMIX ----
+    TRY(launch_tmix_rows(sem, w.x, l == 0 ? b->tokens : nullptr, emb, (const __half*)Lw.ln1_w,
+                         (const __half*)Lw.ln1_b, (const __half*)Lw.mix6, st_tx, b->row_seq,
+                         b->cu_seqlens, b->slots, w.xmix, xl_t, M, C, st));
+    {
+      // r/k/v projections: xmix planes r=0, k=2, v=3
+      rwkv7_gemm_problem p[3] = {
+          {w.xmix + 0 * MC, wrkv + 0 * CC, w.rkv + 0 * MC, nullptr, M, C, C, C, C, C},
+          {w.xmix + 2 * MC, wrkv + 1 * CC, w.rkv + 1 * MC, nullptr, M, C, C, C, C, C},
+          {w.xmix + 3 * MC, wrkv + 2 * CC, w.rkv + 2 * MC, nullptr, M, C, C, C, C, C}};
+      TRY(gemm_launch(p, 3, RWKV_EPI_STORE, st));
+    }
+    {
+      // LoRA down-projections into ranks [M, 288] = v(32) | w(64) | a(64) | g(128)
+      const int R = RWKV_RANK_SUM;
+      rwkv7_gemm_problem p[4] = {
+          {w.xmix + 3 * MC, wdn + 0 * C, w.ranks + 0, nullptr, M, 32, C, C, C, R},
+          {w.xmix + 1 * MC, wdn + 32 * C, w.ranks + 32, nullptr, M, 64, C, C, C, R},
+          {w.xmix + 4 * MC, wdn + 96 * C, w.ranks + 96, nullptr, M, 64, C, C, C, R},
+          {w.xmix + 5 * MC, wdn + 160 * C, w.ranks + 160, nullptr, M, 128, C, C, C, R}};
+      TRY(gemm_launch(p, 4, RWKV_EPI_STORE, st));
+    }
+    TRY(launch_gates(sem, w.ranks, (const __half*)Lw.w_lora_up, w.rkv, (const __half*)Lw.w0,
+                     (const __half*)Lw.a0, (const __half*)Lw.v0, (const __half*)Lw.k_k,
+                     (const __half*)Lw.k_a, w.vfirst, w.gbuf, M, C, l == 0, st));
+    TRY(launch_wkv_tokens(sem, w.rkv, w.gbuf, MC, (const __half*)Lw.r_k, (const __half*)Lw.lnx_w,
+                          (const __half*)Lw.lnx_b, st_rnn, b->cu_seqlens, b->slots, w.yg, S, H, C,
+                          st));
+    {
+      rwkv7_gemm_problem p = {w.yg, Lw.w_o, w.x1, w.x, M, C, C, C, C, C};
+      TRY(gemm_launch(&p, 1, RWKV_EPI_RESID, st));
+    }
+    // ---- CMIX ----
+    TRY(launch_cmix_rows(sem, w.x1, (const __half*)Lw.ln2_w, (const __half*)Lw.ln2_b,
+                         (const __half*)Lw.ffn_x_k, st_cx, b->row_seq, b->cu_seqlens, b->slots,
+                         w.xk, xl_c, M, C, st));
+    {
+      rwkv7_gemm_problem p = {w.xk, Lw.w_fk, w.h, nullptr, M, 4 * C, C, C, C, 4 * C};
+      TRY(gemm_launch(&p, 1, RWKV_EPI_RELUSQ, st));
+    }
+    {
+      rwkv7_gemm_problem p = {w.h, Lw.w_fv, w.x, w.x1, M, C, 4 * C, 4 * C, 4 * C, C};
+      TRY(gemm_launch(&p, 1, RWKV_EPI_RESID, st));
+    }
+  }
+  if (b->n_logits) {
+    TRY(launch_ln_rows(w.x, b->logit_rows, (const __half*)model->lnout_w,
+                       (const __half*)model->lnout_b, w.lnout, b->n_logits, C, st));
+    rwkv7_gemm_problem p = {w.lnout, model->head, b->logits, nullptr, b->n_logits, model->vocab,
+                            C, C, C, model->vocab};
+    TRY(gemm_launch(&p, 1, RWKV_EPI_STORE, st));
+  }
+  TRY(launch_scatter_state_x(w.xlast, (__half*)state->tmix_x, (__half*)state->cmix_x, b->slots, S,
+                             L, ns, C, st));
+  return RWKV_OK;
+}

@@ -1,0 +1,69 @@
+// Shared device helpers for the RWKV-7 sm_100a kernels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/rwkv_b200.h"
+
+#define RWKV_HD 64  // head size N, fixed for RWKV-7
+#define RWKV_RANK_V 32
+#define RWKV_RANK_W 64
+#define RWKV_RANK_A 64
+#define RWKV_RANK_G 128
+#define RWKV_RANK_SUM 288  // v | w | a | g packed order
+
+// Rounding semantics of the two reference paths (see include/rwkv_b200.h).
+enum { SEM_DECODE = 0, SEM_PREFILL = 1 };
+
+__device__ __forceinline__ float r16(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float h2f(__half x) { return __half2float(x); }
+__device__ __forceinline__ __half f2h(float x) { return __float2half_rn(x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// 4 x fp16 <-> float4 through one 8-byte access.
+__device__ __forceinline__ float4 load_h4(const __half* p) {
+  uint2 u = *reinterpret_cast<const uint2*>(p);
+  __half2 a = *reinterpret_cast<__half2*>(&u.x), b = *reinterpret_cast<__half2*>(&u.y);
+  float2 fa = __half22float2(a), fb = __half22float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+__device__ __forceinline__ void store_h4(__half* p, float4 v) {
+  __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// Block-wide sum of NV floats; `red` needs 32*NV floats of shared memory.
+template <int NV>
+__device__ __forceinline__ void block_sum(float (&v)[NV], float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = warp_sum(v[i]);
+  __syncthreads();
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) red[wid * NV + i] = v[i];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += red[w * NV + i];
+    v[i] = s;
+  }
+  __syncthreads();
+}
+
+// Host side: record an error message for rwkv_b200_last_error().
+void rwkv_set_error(const char* fmt, ...);
+int rwkv_check_launch(const char* what);

@@ -1,0 +1,171 @@
+// Row-wise kernels of the token-batch path: LayerNorm + token shift + lerp mixes,
+// the final LayerNorm of logit rows, and the state-x write-back.
+//
+// One CTA per token row, C/4 threads, 4 channels (8 bytes) per thread.
+// Token shift: the previous token of row m is row m-1 when both belong to the
+// same sequence, else the sequence's saved state x (demo/_rwkv7_base.py:228-229).
+#include "common.cuh"
+
+namespace {
+
+// LayerNorm of one row already in registers (4 channels per thread), fp32 math,
+// output rounded to fp16 like F.layer_norm on an fp16 tensor (weight.py:6-15).
+template <int NROW>
+__device__ __forceinline__ void ln_rows(float4 (&x)[NROW], const __half* w, const __half* b, int c,
+                                        int C, float* red) {
+  float s[NROW];
+#pragma unroll
+  for (int i = 0; i < NROW; ++i) s[i] = x[i].x + x[i].y + x[i].z + x[i].w;
+  block_sum<NROW>(s, red);
+  float mean[NROW];
+#pragma unroll
+  for (int i = 0; i < NROW; ++i) {
+    mean[i] = s[i] / C;
+    const float dx = x[i].x - mean[i], dy = x[i].y - mean[i], dz = x[i].z - mean[i],
+                dw = x[i].w - mean[i];
+    s[i] = dx * dx + dy * dy + dz * dz + dw * dw;
+  }
+  block_sum<NROW>(s, red);
+  const float4 ww = load_h4(w + c), bb = load_h4(b + c);
+#pragma unroll
+  for (int i = 0; i < NROW; ++i) {
+    const float rstd = rsqrtf(s[i] / C + 1e-5f);
+    x[i].x = r16((x[i].x - mean[i]) * rstd * ww.x + bb.x);
+    x[i].y = r16((x[i].y - mean[i]) * rstd * ww.y + bb.y);
+    x[i].z = r16((x[i].z - mean[i]) * rstd * ww.z + bb.z);
+    x[i].w = r16((x[i].w - mean[i]) * rstd * ww.w + bb.w);
+  }
+}
+
+// out = x + mu * (prev - x) with the reference's fp16 rounding points.
+template <int SEM>
+__device__ __forceinline__ float lerp_sem(float x, float prev, float mu) {
+  const float diff = r16(prev - x);
+  if (SEM == SEM_DECODE) return r16(x + mu * diff);  // lerp.py:106-114 (fused fp16 fma)
+  return r16(x + r16(mu * diff));                   // _rwkv7_base.py:230-236 (two torch ops)
+}
+
+template <int SEM>
+__device__ __forceinline__ float4 lerp4(float4 x, float4 p, float4 mu) {
+  return make_float4(lerp_sem<SEM>(x.x, p.x, mu.x), lerp_sem<SEM>(x.y, p.y, mu.y),
+                     lerp_sem<SEM>(x.z, p.z, mu.z), lerp_sem<SEM>(x.w, p.w, mu.w));
+}
+
+}  // namespace
+
+// TMIX input stage: [embedding gather] + LN1 + token shift + 6 lerps.
+//   x      : [M, C] layer input (written here when `tokens` != NULL: layer 0 gathers emb rows)
+//   xmix   : 6 x [M, C] = xr, xw, xk, xv, xa, xg
+//   xlast  : [S, C] LN1 output of each sequence's last row (new state x)
+template <int SEM>
+__global__ void k_tmix_rows(__half* __restrict__ x, const int64_t* __restrict__ tokens,
+                            const __half* __restrict__ emb, const __half* __restrict__ ln_w,
+                            const __half* __restrict__ ln_b, const __half* __restrict__ mix6,
+                            const __half* __restrict__ state_x, const int* __restrict__ row_seq,
+                            const int* __restrict__ cu, const int* __restrict__ slots,
+                            __half* __restrict__ xmix, __half* __restrict__ xlast, int M, int C) {
+  __shared__ float red[32 * 2];
+  const int m = blockIdx.x, c = threadIdx.x * 4;
+  const int s = row_seq[m];
+  const bool first = (m == cu[s]), last = (m == cu[s + 1] - 1);
+  float4 v[2];
+  if (tokens) {
+    v[0] = load_h4(emb + (size_t)tokens[m] * C + c);
+    v[1] = first ? v[0] : load_h4(emb + (size_t)tokens[m - 1] * C + c);
+    store_h4(x + (size_t)m * C + c, v[0]);
+  } else {
+    v[0] = load_h4(x + (size_t)m * C + c);
+    v[1] = first ? v[0] : load_h4(x + (size_t)(m - 1) * C + c);
+  }
+  ln_rows<2>(v, ln_w, ln_b, c, C, red);
+  const int slot = slots ? slots[s] : s;
+  const float4 prev = first ? load_h4(state_x + (size_t)slot * C + c) : v[1];
+  const size_t plane = (size_t)M * C;
+#pragma unroll
+  for (int j = 0; j < 6; ++j)
+    store_h4(xmix + j * plane + (size_t)m * C + c, lerp4<SEM>(v[0], prev, load_h4(mix6 + j * C + c)));
+  if (last) store_h4(xlast + (size_t)s * C + c, v[0]);
+}
+
+// CMIX input stage: LN2 + token shift + one lerp (x_k).
+template <int SEM>
+__global__ void k_cmix_rows(const __half* __restrict__ x, const __half* __restrict__ ln_w,
+                            const __half* __restrict__ ln_b, const __half* __restrict__ mu,
+                            const __half* __restrict__ state_x, const int* __restrict__ row_seq,
+                            const int* __restrict__ cu, const int* __restrict__ slots,
+                            __half* __restrict__ xk, __half* __restrict__ xlast, int C) {
+  __shared__ float red[32 * 2];
+  const int m = blockIdx.x, c = threadIdx.x * 4;
+  const int s = row_seq[m];
+  const bool first = (m == cu[s]), last = (m == cu[s + 1] - 1);
+  float4 v[2];
+  v[0] = load_h4(x + (size_t)m * C + c);
+  v[1] = first ? v[0] : load_h4(x + (size_t)(m - 1) * C + c);
+  ln_rows<2>(v, ln_w, ln_b, c, C, red);
+  const int slot = slots ? slots[s] : s;
+  const float4 prev = first ? load_h4(state_x + (size_t)slot * C + c) : v[1];
+  store_h4(xk + (size_t)m * C + c, lerp4<SEM>(v[0], prev, load_h4(mu + c)));
+  if (last) store_h4(xlast + (size_t)s * C + c, v[0]);
+}
+
+// ln_out of the rows that produce logits: out[i] = LN(x[rows[i]]).
+__global__ void k_ln_rows(const __half* __restrict__ x, const int* __restrict__ rows,
+                          const __half* __restrict__ w, const __half* __restrict__ b,
+                          __half* __restrict__ out, int C) {
+  __shared__ float red[32];
+  const int i = blockIdx.x, c = threadIdx.x * 4;
+  float4 v[1];
+  v[0] = load_h4(x + (size_t)rows[i] * C + c);
+  ln_rows<1>(v, w, b, c, C, red);
+  store_h4(out + (size_t)i * C + c, v[0]);
+}
+
+// New state x of every layer: tmix_x[l][slot] = xlast[l][0][s], cmix_x[l][slot] = xlast[l][1][s].
+// grid = (S, L, 2), block = C/4.
+__global__ void k_scatter_state_x(const __half* __restrict__ xlast, __half* __restrict__ tmix_x,
+                                  __half* __restrict__ cmix_x, const int* __restrict__ slots,
+                                  int S, int n_slots, int C) {
+  const int s = blockIdx.x, l = blockIdx.y, which = blockIdx.z, c = threadIdx.x * 4;
+  const int slot = slots ? slots[s] : s;
+  const __half* src = xlast + (((size_t)l * 2 + which) * S + s) * C + c;
+  __half* dst = (which ? cmix_x : tmix_x) + ((size_t)l * n_slots + slot) * C + c;
+  *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
+}
+
+int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* emb,
+                     const __half* ln_w, const __half* ln_b, const __half* mix6,
+                     const __half* state_x, const int* row_seq, const int* cu, const int* slots,
+                     __half* xmix, __half* xlast, int M, int C, cudaStream_t st) {
+  if (sem == SEM_DECODE)
+    k_tmix_rows<SEM_DECODE><<<M, C / 4, 0, st>>>(x, tokens, emb, ln_w, ln_b, mix6, state_x, row_seq,
+                                                 cu, slots, xmix, xlast, M, C);
+  else
+    k_tmix_rows<SEM_PREFILL><<<M, C / 4, 0, st>>>(x, tokens, emb, ln_w, ln_b, mix6, state_x,
+                                                  row_seq, cu, slots, xmix, xlast, M, C);
+  return rwkv_check_launch("tmix_rows");
+}
+
+int launch_cmix_rows(int sem, const __half* x, const __half* ln_w, const __half* ln_b,
+                     const __half* mu, const __half* state_x, const int* row_seq, const int* cu,
+                     const int* slots, __half* xk, __half* xlast, int M, int C, cudaStream_t st) {
+  if (sem == SEM_DECODE)
+    k_cmix_rows<SEM_DECODE><<<M, C / 4, 0, st>>>(x, ln_w, ln_b, mu, state_x, row_seq, cu, slots, xk,
+                                                 xlast, C);
+  else
+    k_cmix_rows<SEM_PREFILL><<<M, C / 4, 0, st>>>(x, ln_w, ln_b, mu, state_x, row_seq, cu, slots,
+                                                  xk, xlast, C);
+  return rwkv_check_launch("cmix_rows");
+}
+
+int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __half* b,
+                   __half* out, int n, int C, cudaStream_t st) {
+  if (n == 0) return RWKV_OK;
+  k_ln_rows<<<n, C / 4, 0, st>>>(x, rows, w, b, out, C);
+  return rwkv_check_launch("ln_rows");
+}
+
+int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,
+                           int S, int L, int n_slots, int C, cudaStream_t st) {
+  k_scatter_state_x<<<dim3(S, L, 2), C / 4, 0, st>>>(xlast, tmix_x, cmix_x, slots, S, n_slots, C);
+  return rwkv_check_launch("scatter_state_x");
+}

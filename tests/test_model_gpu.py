@@ -1,0 +1,177 @@
+"""End-to-end parity of the B200 model against the fp16 CPU oracle.
+
+Mirrors the reference's ``test/test_forward.py`` cases (decode per token,
+prefill + last-token decode) on seeded synthetic checkpoints, at the north
+star's tolerance (logits max-abs 2e-2, relative-L2 1e-3; wkv state relative
+1e-3; greedy argmax), plus the batched (many-sequence) entry points.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle.rwkv7_oracle import OracleState, OracleWeights, RWKV7Oracle
+from rwkv_tl_b200 import BatchedState, RWKV7B200, RWKV7Weight, State, make_rwkv7
+from rwkv_tl_b200.synth import CONFIG_0_1B, CONFIG_0_4B, CONFIG_TINY, synth_checkpoint
+from tests._util import assert_logits_close, assert_state_close, gpu_state_to_oracle
+
+pytestmark = pytest.mark.gpu
+
+_CACHE: dict = {}
+
+
+def _pair(cfg, seed):
+    key = (cfg, seed)
+    if key not in _CACHE:
+        sd = synth_checkpoint(cfg, seed=seed)
+        w = RWKV7Weight(sd, device="cuda")
+        _CACHE.clear()
+        _CACHE[key] = (RWKV7B200(w), RWKV7Oracle(OracleWeights(sd, mode="fp16")))
+    return _CACHE[key]
+
+
+def _tokens(n, V, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, V, (n,), generator=g).tolist()
+
+
+def test_tiny_decode_per_token():
+    m, o = _pair(CONFIG_TINY, 1)
+    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    for i, t in enumerate(_tokens(12, CONFIG_TINY.vocab, 0)):
+        lg, S = m.decode(torch.tensor([t], device="cuda"), S)
+        assert_logits_close(lg.float(), o.decode(t, So), f"step {i}")
+    assert_state_close(S, So, "tiny decode")
+
+
+def test_tiny_forward_prefill_then_decode():
+    m, o = _pair(CONFIG_TINY, 1)
+    toks = _tokens(33, CONFIG_TINY.vocab, 1)
+    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    lg, S = m.forward(torch.tensor(toks, device="cuda"), S)
+    assert_logits_close(lg.float(), o.forward(toks, So), "forward")
+    assert_state_close(S, So, "tiny forward")
+
+
+def test_prefill_chunking_matches_single_call():
+    m, _ = _pair(CONFIG_TINY, 1)
+    toks = torch.tensor(_tokens(50, CONFIG_TINY.vocab, 2), device="cuda")
+    S1 = State(m.L, m.C, 64, device="cuda")
+    m.prefill(toks, S1)
+    m2 = RWKV7B200(m.w, max_rows=16)
+    S2 = State(m.L, m.C, 64, device="cuda")
+    m2.prefill(toks, S2)
+    for a, b in zip(S1.tmix, S2.tmix):
+        assert torch.equal(a["rnn"], b["rnn"]) and torch.equal(a["x"], b["x"])
+
+
+def test_cfg0_greedy_0p1b():
+    """BASELINE config 0 workload on the GPU path: 0.1B, 8-token prompt, 16 greedy steps."""
+    m, o = _pair(CONFIG_0_1B, 0)
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, 65536, (8,), generator=g).tolist()
+    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    lg, S = m.forward(torch.tensor(prompt, device="cuda"), S)
+    olg = o.forward(prompt, So)
+    assert_logits_close(lg.float(), olg, "prompt")
+    agree = 0
+    for step in range(16):
+        tok = int(olg.argmax())
+        agree += int(lg.float().argmax()) == tok
+        if step == 15:
+            break
+        lg, S = m.decode(torch.tensor([tok], device="cuda"), S)
+        olg = o.decode(tok, So)
+        assert_logits_close(lg.float(), olg, f"greedy step {step}")
+    assert agree >= 16  # >= 99% of 16 steps
+    assert_state_close(S, So, "cfg0 state")
+
+
+def test_0p4b_prefill64_and_decode():
+    m, o = _pair(CONFIG_0_4B, 0)
+    toks = _tokens(64, 65536, 3)
+    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    lg, S = m.forward(torch.tensor(toks, device="cuda"), S)
+    assert_logits_close(lg.float(), o.forward(toks, So), "0.4B forward")
+    for i, t in enumerate(_tokens(3, 65536, 4)):
+        lg, S = m.decode(torch.tensor([t], device="cuda"), S)
+        assert_logits_close(lg.float(), o.decode(t, So), f"0.4B decode {i}")
+    assert_state_close(S, So, "0.4B state")
+
+
+def test_decode_batch_random_states():
+    """Config 2 style: one decode step of B sequences from random states."""
+    m, o = _pair(CONFIG_TINY, 1)
+    B = 5
+    bs = BatchedState(m.L, m.C, B, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    bs.rnn.copy_(0.1 * torch.randn(bs.rnn.shape, generator=g, device="cuda"))
+    bs.tmix_x.copy_(torch.randn(bs.tmix_x.shape, generator=g, device="cuda").half())
+    bs.cmix_x.copy_(torch.randn(bs.cmix_x.shape, generator=g, device="cuda").half())
+    toks = _tokens(B, CONFIG_TINY.vocab, 6)
+    oracle_states = []
+    for b in range(B):
+        So = OracleState(o.w.L, o.w.C)
+        gpu_state_to_oracle(bs[b], So)
+        oracle_states.append(So)
+    lg = m.decode_batch(torch.tensor(toks, device="cuda"), bs)
+    for b in range(B):
+        assert_logits_close(lg[b].float(), o.decode(toks[b], oracle_states[b]), f"seq {b}")
+        assert_state_close(bs[b], oracle_states[b], f"seq {b}")
+
+
+def test_prefill_batch_varlen_and_slots():
+    m, o = _pair(CONFIG_TINY, 1)
+    lens = [1, 7, 20, 3]
+    seqs = [_tokens(n, CONFIG_TINY.vocab, 10 + i) for i, n in enumerate(lens)]
+    bs = BatchedState(m.L, m.C, 6, device="cuda")
+    slots = [5, 0, 3, 1]
+    lg = m.forward_batch([torch.tensor(s) for s in seqs], bs, slots)
+    for i, s in enumerate(seqs):
+        So = OracleState(o.w.L, o.w.C)
+        assert_logits_close(lg[i].float(), o.forward(s, So), f"seq {i}")
+        assert_state_close(bs[slots[i]], So, f"seq {i}")
+    # untouched slots stay zero
+    assert bs.rnn[:, 2].abs().max() == 0 and bs.rnn[:, 4].abs().max() == 0
+
+
+def test_graph_wrapper_matches_eager():
+    m, _ = _pair(CONFIG_TINY, 1)
+    cls = make_rwkv7(torch.device("cuda"), backend="b200")
+    gm = cls(m.w)
+    toks = _tokens(40, CONFIG_TINY.vocab, 7)
+    S1, S2 = State(m.L, m.C, 64, device="cuda"), State(m.L, m.C, 64, device="cuda")
+    for chunk in (toks[:9], toks[9:30]):
+        m.prefill(torch.tensor(chunk, device="cuda"), S1)
+        gm.prefill(torch.tensor(chunk, device="cuda"), S2)
+    for t in toks[30:]:
+        a, _ = m.decode(torch.tensor([t], device="cuda"), S1)
+        b, _ = gm.decode(torch.tensor(t, device="cuda"), S2)
+        assert torch.equal(a, b)
+    for x, y in zip(S1.tmix, S2.tmix):
+        assert torch.equal(x["rnn"], y["rnn"])
+
+
+def test_foreign_state_layout_roundtrip():
+    """A State whose dict entries were rebound still works (staged copy in/out)."""
+    m, o = _pair(CONFIG_TINY, 1)
+    S = State(m.L, m.C, 64, device="cuda")
+    for d in S.tmix:
+        d["rnn"] = d["rnn"].clone()  # rebind: no longer aliases the blocks
+    So = OracleState(o.w.L, o.w.C)
+    for t in _tokens(4, CONFIG_TINY.vocab, 8):
+        lg, S = m.decode(t, S)
+        assert_logits_close(lg.float(), o.decode(t, So), "foreign")
+    assert_state_close(S, So, "foreign")
+
+
+def test_errors():
+    m, _ = _pair(CONFIG_TINY, 1)
+    S = State(m.L, m.C, 64, device="cuda")
+    with pytest.raises(RuntimeError):
+        m.prefill(torch.tensor([], dtype=torch.long, device="cuda"), S)
+    with pytest.raises(ValueError):
+        m.forward(torch.zeros(2, 2, dtype=torch.long, device="cuda"), S)
+    with pytest.raises(ValueError):
+        make_rwkv7(torch.device("cuda"), backend="nope")

@@ -1,0 +1,86 @@
+"""wkv7 DPLR kernels vs the CPU oracle recurrence (BASELINE config 1 shapes/inits)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle.rwkv7_oracle import RWKV7Oracle
+
+from tests._util import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(B, T, H, seed):
+    """Config-1 inits: r,k,v ~ N(0,1); k_hat = k/|k|; a = sigmoid(N); w = exp(-0.606531 sigmoid(N));
+    A = k_hat, B = -k_hat * a; S0 = 0.1 N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    r = torch.randn(B, T, H, 64, generator=g)
+    k = torch.randn(B, T, H, 64, generator=g)
+    v = torch.randn(B, T, H, 64, generator=g)
+    a = torch.sigmoid(torch.randn(B, T, H, 64, generator=g))
+    w = torch.exp(-0.606531 * torch.sigmoid(torch.randn(B, T, H, 64, generator=g)))
+    kh = k / k.norm(dim=-1, keepdim=True)
+    S0 = 0.1 * torch.randn(B, H, 64, 64, generator=g)
+    h = lambda t: t.half()  # noqa: E731
+    return h(r), h(w), h(k), h(v), h(kh), h(-kh * a), S0
+
+
+def _ref(S0, r, w, k, v, A, B):
+    """Serial recurrence in fp32 on the fp16-rounded inputs."""
+    S = S0.clone()
+    T = r.shape[1]
+    ys = []
+    for t in range(T):
+        y, S = zip(*[RWKV7Oracle._wkv_step(S[b], r[b, t].float(), w[b, t].float(), k[b, t].float(),
+                                           v[b, t].float(), A[b, t].float(), B[b, t].float())
+                     for b in range(S.shape[0])])
+        S = torch.stack(S)
+        ys.append(torch.stack(y))
+    return torch.stack(ys, 1), S
+
+
+@pytest.mark.parametrize("B", [1, 8, 64])
+def test_dplr_step_batched(B):
+    from rwkv_tl_b200 import _lib
+
+    lib = _lib.load()
+    H = 16
+    r, w, k, v, A, Bv, S0 = _inputs(B, 1, H, seed=B)
+    yref, Sref = _ref(S0, r, w, k, v, A, Bv)
+    dev = [t[:, 0].contiguous().cuda() for t in (r, w, k, v, A, Bv)]
+    S = S0.cuda().contiguous()
+    y = torch.empty(B, H, 64, dtype=torch.float16, device="cuda")
+    _lib.check(lib.rwkv7_dplr_step(S.data_ptr(), *[t.data_ptr() for t in dev], y.data_ptr(), B, H,
+                                   torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert rel_l2(S, Sref) < 1e-5
+    assert (y.float().cpu() - yref[:, 0]).abs().max() <= 2e-3 * max(1.0, yref.abs().max())
+
+
+@pytest.mark.parametrize("T", [1, 64, 1024])
+def test_dplr_seq(T):
+    from rwkv_tl_b200 import _lib
+
+    lib = _lib.load()
+    H = 16
+    r, w, k, v, A, Bv, S0 = _inputs(1, T, H, seed=T)
+    yref, Sref = _ref(S0, r, w, k, v, A, Bv)
+    dev = [t[0].contiguous().cuda() for t in (r, w, k, v, A, Bv)]
+    S = S0[0].cuda().contiguous()
+    y = torch.empty(T, H, 64, dtype=torch.float16, device="cuda")
+    _lib.check(lib.rwkv7_dplr_seq(S.data_ptr(), *[t.data_ptr() for t in dev], y.data_ptr(), T, H,
+                                  torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert rel_l2(S, Sref[0]) < 1e-4
+    assert rel_l2(y.float(), yref[0]) < 2e-3
+
+
+def test_dplr_rejects_bad_args():
+    from rwkv_tl_b200 import _lib
+
+    lib = _lib.load()
+    rc = lib.rwkv7_dplr_step(None, None, None, None, None, None, None, None, 1, 16, None)
+    assert rc == _lib.RWKV_ERR_ARG
+    assert b"rwkv7_dplr_step" in lib.rwkv_b200_last_error()
