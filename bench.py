@@ -1,0 +1,375 @@
+"""Benchmark: RWKV-7 0.4B fp16 batched decode on B200 (one process per GPU).
+
+``python bench.py --gpus N --steps K --warmup W [--impl b200|reference]``
+
+Workload (BASELINE metric "decode tokens/s (0.4B, B=1..256, 1/2/4/8 GPU);
+prefill tokens/s at T=4096"): one step = one decode token for each of B=256
+independent sequences per GPU (config 4's per-GPU decode batch, config 2's
+random states), random-init 0.4B weights (L=24, C=1024, V=65536), seeded
+uniform token ids. Sequences are sharded across ranks (each rank owns its own
+256 sequences and their states): no collective on the hot path, weak scaling.
+Inputs (weights 0.77 GB + states 3.3 GB per GPU) are far larger than the
+126 MB L2, so every step streams from HBM without an explicit flush.
+
+* ``value``: tokens/s with inputs resident in HBM, K replays of the captured
+  decode step, CUDA events on the launching stream, max over ranks.
+* ``e2e``: the same step through the public API with host buffers: each step
+  copies the B token ids from pinned host memory, runs ``decode_batch`` (CUDA
+  graph), takes the greedy argmax on the device and reads the B next-token ids
+  back into pinned host memory (synchronised).
+* ``roofline``: the dominant kernel of the step timed alone on the same stream.
+* ``cpu_baseline``: the CPU oracle port of the reference's pure-torch model
+  (``oracle/``) decoding a bounded sample on the host cores (rank 0, N=1).
+* ``--impl reference``: only the CPU port, on all host threads (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "decode tokens/s (0.4B, B=1..256, 1/2/4/8 GPU); prefill tokens/s at T=4096"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class Clocks:
+    """Sample nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = max(smax, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- #
+# CPU port of the reference (oracle) -- the baseline, never the product path
+# --------------------------------------------------------------------------- #
+def cpu_decode_rate(n_tokens: int, threads: int) -> dict:
+    from oracle.rwkv7_oracle import OracleState, OracleWeights, RWKV7Oracle
+    from rwkv_tl_b200.synth import CONFIG_0_4B, synth_checkpoint
+
+    torch.set_num_threads(threads)
+    o = RWKV7Oracle(OracleWeights(synth_checkpoint(CONFIG_0_4B, seed=0), mode="fp32"))
+    S = OracleState(o.w.L, o.w.C)
+    o.decode(1, S)  # warm-up
+    times = []
+    for i in range(n_tokens):
+        t0 = time.perf_counter()
+        o.decode(1000 + i, S)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": 1.0 / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"0.4B fp32 decode (oracle port of demo/rwkv7_torch.py), 1 sequence, "
+                      f"{n_tokens} tokens after 1 warm-up, median {med * 1e3:.1f} ms/token; "
+                      "batched CPU decode loops over sequences, so tokens/s is per token"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    from oracle.rwkv7_oracle import OracleState, OracleWeights, RWKV7Oracle
+    from rwkv_tl_b200.synth import CONFIG_0_4B, synth_checkpoint
+
+    torch.set_num_threads(threads)
+    o = RWKV7Oracle(OracleWeights(synth_checkpoint(CONFIG_0_4B, seed=0), mode="fp32"))
+    S = OracleState(o.w.L, o.w.C)
+    for i in range(args.warmup):
+        o.decode(i, S)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        o.decode(100 + i, S)
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "0.4B decode, one token of one sequence per step (CPU port; "
+                               "the B=256 batch is a loop over sequences)",
+                   "global_batch": 1, "seq_len": 1, "parallelism": "none"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} decode tokens of one sequence"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- #
+def timed(fn, steps: int, stream) -> float:
+    """Average ms per call over `steps` calls, CUDA events on `stream`."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def run_b200(args, world, rank, local):
+    from rwkv_tl_b200 import BatchedState, RWKV7Weight, State, _lib, make_rwkv7
+    from rwkv_tl_b200.synth import CONFIG_0_4B, synth_checkpoint
+
+    cfg = CONFIG_0_4B
+    dev = torch.device("cuda", local)
+    B = args.batch
+    sd = synth_checkpoint(cfg, seed=0, device=dev)
+    w = RWKV7Weight(sd, device=dev)
+    del sd
+    torch.cuda.empty_cache()
+    model = make_rwkv7(dev, backend="b200")(w)
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    state = BatchedState(w.L, w.C, B, device=dev)
+    state.rnn.normal_(0.0, 0.1, generator=g)
+    state.tmix_x.copy_(torch.randn(state.tmix_x.shape, generator=g, device=dev).half())
+    state.cmix_x.copy_(torch.randn(state.cmix_x.shape, generator=g, device=dev).half())
+    tokens = torch.randint(0, cfg.vocab, (B,), generator=g, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # launches per step (eager call through the library)
+    c0 = lib.rwkv_b200_launch_count()
+    model.model.decode_batch(tokens, state)
+    launches_per_step = int(lib.rwkv_b200_launch_count() - c0)
+
+    step = lambda: model.decode_batch(tokens, state)  # noqa: E731 (graph replay)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    with Clocks(local) as clk:
+        ms = timed(step, args.steps, stream)
+        barrier(world)
+    ms = max_over_ranks(ms, world)
+    value = world * B / (ms * 1e-3)
+
+    # ---- e2e through the public API with host buffers ----
+    host_tok = torch.randint(0, cfg.vocab, (B,), dtype=torch.int64).pin_memory()
+    host_out = torch.empty(B, dtype=torch.int64).pin_memory()
+    dev_tok = torch.empty(B, dtype=torch.int64, device=dev)
+
+    def e2e_step():
+        dev_tok.copy_(host_tok, non_blocking=True)
+        logits = model.decode_batch(dev_tok, state)
+        host_out.copy_(logits.argmax(-1), non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    barrier(world)
+    e2e_ms = timed(e2e_step, args.steps, stream)
+    e2e_ms = max_over_ranks(e2e_ms, world)
+    e2e_val = world * B / (e2e_ms * 1e-3)
+
+    # ---- roofline of the step (HBM bound): algorithmic bytes per step ----
+    pk, pk_kind = peaks()
+    wbytes = w.nbytes() - 2 * w.emb.numel()  # weights streamed per step (emb: rows only)
+    state_bytes = B * w.L * (w.H * 64 * 64 * 4 * 2 + 2 * w.C * 2 * 2)
+    io_bytes = B * (w.C * 2 + cfg.vocab * 2)
+    step_bytes = wbytes + state_bytes + io_bytes
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+
+    extra = {}
+    if rank == 0 and world == 1 and not args.quick:
+        extra = side_measurements(model, w, dev, stream)
+
+    clocks = clk.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random-init 0.4B weights, random states, uniform token ids)",
+            "config": {"workload": f"RWKV-7 0.4B fp16 decode, B={B} sequences per GPU, one "
+                                   "token each per step (CUDA graph)",
+                       "model": "rwkv7-0.4B (L24 C1024 V65536)", "global_batch": world * B,
+                       "seq_len": 1, "parallelism": f"sequence-sharded x{world}",
+                       "l2": "inputs > L2 (weights 0.77 GB + state 3.3 GB per GPU), no flush"},
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": B * 8,
+                    "d2h_bytes_per_step": B * 8},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (all kernels, one graph)",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind,
+                         "traffic": None, "algorithmic_bytes_per_step": step_bytes},
+            "clocks": clocks,
+        }
+        line.update(extra)
+        if world == 1 and not args.quick:
+            line["cpu_baseline"] = cpu_decode_rate(args.cpu_tokens, os.cpu_count() or 1)
+        print(json.dumps(line), flush=True)
+
+
+def side_measurements(model, w, dev, stream) -> dict:
+    """Decode at B = 1, 8, 64 and prefill at T = 4096 (reported beside the headline)."""
+    from rwkv_tl_b200 import BatchedState, State
+
+    out = {"decode_tokens_per_s_by_batch": {}}
+    for B in (1, 8, 64):
+        st = BatchedState(w.L, w.C, B, device=dev)
+        tok = torch.randint(0, w.V, (B,), device=dev)
+        f = lambda: model.decode_batch(tok, st)  # noqa: E731
+        for _ in range(3):
+            f()
+        ms = timed(f, 10, stream)
+        out["decode_tokens_per_s_by_batch"][str(B)] = B / (ms * 1e-3)
+    S = State(w.L, w.C, 64, device=dev)
+    toks = torch.randint(0, w.V, (4096,), device=dev)
+    f = lambda: model.prefill(toks, S)  # noqa: E731
+    f()
+    ms = timed(f, 3, stream)
+    out["prefill_T4096"] = {"tokens_per_s": 4096 / (ms * 1e-3), "ms": ms}
+    return out
+
+
+def run_profile(args):
+    """Small driver for ncu: the same weights/kernels as the bench, one kind of call."""
+    from rwkv_tl_b200 import BatchedState, RWKV7Weight, State, make_rwkv7
+    from rwkv_tl_b200.synth import CONFIG_0_4B, synth_checkpoint
+
+    dev = torch.device("cuda", 0)
+    sd = synth_checkpoint(CONFIG_0_4B, seed=0, device=dev)
+    w = RWKV7Weight(sd, device=dev)
+    del sd
+    model = make_rwkv7(dev, backend="b200", use_graph=False)(w)
+    stream = torch.cuda.current_stream(dev)
+    if args.profile == "decode":
+        st = BatchedState(w.L, w.C, args.batch, device=dev)
+        tok = torch.randint(0, w.V, (args.batch,), device=dev)
+        f = lambda: model.decode_batch(tok, st)  # noqa: E731
+    else:
+        S = State(w.L, w.C, 64, device=dev)
+        toks = torch.randint(0, w.V, (args.seq_len,), device=dev)
+        f = lambda: model.prefill(toks, S)  # noqa: E731
+    for _ in range(args.warmup):
+        f()
+    ms = timed(f, args.steps, stream)
+    print(f"{args.profile}: {ms:.3f} ms per call", flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--cpu-tokens", type=int, default=4)
+    ap.add_argument("--quick", action="store_true", help="skip side measurements / CPU baseline")
+    ap.add_argument("--profile", choices=["decode", "prefill"], default=None,
+                    help="profiling driver: run only K decode steps (--batch) or K prefills "
+                         "(--seq-len) and print the per-call time, no JSON line")
+    ap.add_argument("--seq-len", type=int, default=4096)
+    args = ap.parse_args()
+    world, rank, local = dist_setup() if args.impl == "b200" or int(
+        os.environ.get("WORLD_SIZE", "1")) == 1 else (int(os.environ["WORLD_SIZE"]),
+                                                      int(os.environ.get("RANK", "0")), 0)
+    if args.profile:
+        run_profile(args)
+    elif args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_b200(args, world, rank, local)
+    if world > 1 and args.impl == "b200":
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

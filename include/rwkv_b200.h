@@ -16,6 +16,7 @@
  *   rwkv7_dplr_step     <- Kernels.fused_dplr      src/rwkv_tl/kernels/dplr.py:256-270
  *                          (torch.ops.rwkv_tl.fused_dplr, src/rwkv_tl/operators/__init__.py:315-322)
  *   rwkv7_dplr_seq      <- Kernels.fused_dplr_T    src/rwkv_tl/kernels/dplr.py:272-285
+ *   rwkv7_dplr_chunked  <- Kernels.fused_dplr_T (chunk-parallel, batched over sequences)
  *   rwkv7_gemm_f16      <- Kernels.fused_rkv_gemm / ffn_h / ffn_v / out_mm
  *                          src/rwkv_tl/kernels/gemm.py:215-305
  *   rwkv7_forward       <- RWKV7Base.prefill / RWKV7Base.decode layer loops
@@ -112,6 +113,9 @@ typedef struct rwkv7_batch {
 
 const char* rwkv_b200_last_error(void);
 int rwkv_b200_abi_version(void);
+/* Number of kernel launches this library has issued from the host so far (a
+ * captured CUDA graph replays its kernels without passing through here). */
+unsigned long long rwkv_b200_launch_count(void);
 
 /* wkv7 DPLR step, batched over n_seq independent sequences (T = 1):
  *   sa[v] = sum_j S[v,j] a[j];  S[v,k] = S[v,k] w[k] + sa[v] b[k] + v[v] k[k];
@@ -125,6 +129,15 @@ int rwkv7_dplr_step(void* S, const void* r, const void* w, const void* k, const 
  * r..b, y: fp16 [T, H, 64]; S: fp32 [H, 64, 64] updated in place. */
 int rwkv7_dplr_seq(void* S, const void* r, const void* w, const void* k, const void* v,
                    const void* a, const void* b, void* y, int T, int H, void* stream);
+
+/* Chunk-parallel form of the same recurrence for n_seq sequences of T tokens
+ * (replaces fused_dplr_T's serial loop for long T):
+ * r..b, y: fp16 [n_seq, T, H, 64]; S: fp32 [n_seq, H, 64, 64] updated in place.
+ * Needs rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H) bytes of scratch. */
+size_t rwkv7_dplr_chunked_workspace_bytes(int n_seq, int T, int H);
+int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const void* k, const void* v,
+                       const void* a, const void* b, void* y, int n_seq, int T, int H,
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* Grouped fp16 GEMM, up to 4 independent problems in one launch:
  *   C_g[M_g, N_g] = epi( A_g[M_g, K_g] @ B_g[N_g, K_g]^T )

@@ -46,8 +46,8 @@ LN_EPS = 1e-5  # F.layer_norm default, weight.py:15
 
 
 def _r16(x: Tensor) -> Tensor:
-    """Round an fp32 tensor to fp16 precision and back (one fp16 store)."""
-    return x.to(torch.float16).to(torch.float32)
+    """Round to fp16 precision and back to the compute dtype (one fp16 store)."""
+    return x.to(torch.float16).to(x.dtype)
 
 
 class OracleWeights:
@@ -59,12 +59,14 @@ class OracleWeights:
     projections in ``[in, out]`` orientation (``weight.py:98-106,124-126``).
     """
 
-    def __init__(self, sd: dict[str, Tensor], mode: str = "fp16"):
+    def __init__(self, sd: dict[str, Tensor], mode: str = "fp16",
+                 compute_dtype: torch.dtype = torch.float32):
         if mode not in ("fp16", "fp32"):
             raise ValueError(mode)
         self.mode = mode
+        self.compute_dtype = compute_dtype
         q = _r16 if mode == "fp16" else (lambda t: t)
-        W = {k: q(v.detach().to("cpu", torch.float32)) for k, v in sd.items()}
+        W = {k: q(v.detach().to("cpu", compute_dtype)) for k, v in sd.items()}
         self.C = W["emb.weight"].shape[1]
         self.V = W["emb.weight"].shape[0]
         self.L = 1 + max(int(k.split(".")[1]) for k in W if k.startswith("blocks."))
@@ -101,11 +103,11 @@ class OracleWeights:
 class OracleState:
     """Per-sequence state with the layout of ``src/rwkv_tl/state.py:31-44``."""
 
-    def __init__(self, L: int, C: int, *, zero: bool = True):
+    def __init__(self, L: int, C: int, *, dtype: torch.dtype = torch.float32):
         H = C // 64
-        self.tmix_x = [torch.zeros(C) for _ in range(L)]
-        self.rnn = [torch.zeros(H, 64, 64) for _ in range(L)]
-        self.cmix_x = [torch.zeros(C) for _ in range(L)]
+        self.tmix_x = [torch.zeros(C, dtype=dtype) for _ in range(L)]
+        self.rnn = [torch.zeros(H, 64, 64, dtype=dtype) for _ in range(L)]
+        self.cmix_x = [torch.zeros(C, dtype=dtype) for _ in range(L)]
 
     def clone(self) -> "OracleState":
         s = OracleState.__new__(OracleState)
@@ -270,7 +272,7 @@ class RWKV7Oracle:
         den = q(torch.sqrt(q(q(kk3 * kk3).sum(-1, keepdim=True))))
         kn = q(kk3 / torch.clamp(den, min=1e-12))
         B = q(-kn * a3)
-        y = torch.empty(T, H, 64)
+        y = torch.empty(T, H, 64, dtype=x0.dtype)
         St = S.rnn[i]
         for t in range(T):
             yt, St = self._wkv_step(St, r3[t], w3[t], k3[t], v3[t], kn[t], B[t])

@@ -17,8 +17,11 @@ LIB_PATH = Path(os.environ.get("RWKV_B200_LIB", _PKG / "librwkv_b200.so"))
 EXPORTED = (
     "rwkv_b200_last_error",
     "rwkv_b200_abi_version",
+    "rwkv_b200_launch_count",
     "rwkv7_dplr_step",
     "rwkv7_dplr_seq",
+    "rwkv7_dplr_chunked_workspace_bytes",
+    "rwkv7_dplr_chunked",
     "rwkv7_gemm_f16",
     "rwkv7_forward_workspace_bytes",
     "rwkv7_forward",
@@ -93,10 +96,15 @@ def load() -> C.CDLL:
     lib = C.CDLL(str(LIB_PATH))
     lib.rwkv_b200_last_error.restype = C.c_char_p
     lib.rwkv_b200_abi_version.restype = C.c_int
+    lib.rwkv_b200_launch_count.restype = C.c_ulonglong
     for name in ("rwkv7_dplr_step", "rwkv7_dplr_seq"):
         f = getattr(lib, name)
         f.restype = C.c_int
         f.argtypes = [vp] * 8 + [C.c_int, C.c_int, vp]
+    lib.rwkv7_dplr_chunked_workspace_bytes.restype = C.c_size_t
+    lib.rwkv7_dplr_chunked_workspace_bytes.argtypes = [C.c_int, C.c_int, C.c_int]
+    lib.rwkv7_dplr_chunked.restype = C.c_int
+    lib.rwkv7_dplr_chunked.argtypes = [vp] * 8 + [C.c_int] * 3 + [vp, C.c_size_t, vp]
     lib.rwkv7_gemm_f16.restype = C.c_int
     lib.rwkv7_gemm_f16.argtypes = [C.POINTER(GemmProblem), C.c_int, C.c_int, vp]
     lib.rwkv7_forward_workspace_bytes.restype = C.c_size_t

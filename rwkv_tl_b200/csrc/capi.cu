@@ -8,6 +8,7 @@
 // requested rows and the state-x write-back.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -20,7 +21,10 @@ void rwkv_set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+static unsigned long long g_launches = 0;  // kernels launched by this library (host side)
+
 int rwkv_check_launch(const char* what) {
+  __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     rwkv_set_error("%s: CUDA error %s", what, cudaGetErrorString(e));
@@ -31,6 +35,9 @@ int rwkv_check_launch(const char* what) {
 
 extern "C" const char* rwkv_b200_last_error(void) { return g_err; }
 extern "C" int rwkv_b200_abi_version(void) { return RWKV_B200_ABI_VERSION; }
+extern "C" unsigned long long rwkv_b200_launch_count(void) {
+  return __atomic_load_n(&g_launches, __ATOMIC_RELAXED);
+}
 
 // launchers from the other translation units
 int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* emb,
@@ -53,6 +60,14 @@ int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t pl
                       const int* cu, const int* slots, __half* yg, int n_seqs, int H, int C,
                       cudaStream_t st);
 int gemm_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStream_t st);
+size_t wkv_chunk_record_bytes(int M, int S, int H);
+int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
+                       const __half* a, const __half* b, float* rnn, const int* cu,
+                       const int* slots, __half* ybuf, float* rec, int* chunk_cu, int M, int S,
+                       int H, cudaStream_t st);
+int launch_wkv_epilogue(int sem, const __half* ybuf, const __half* rbuf, const __half* gbuf,
+                        size_t plane, const __half* r_k, const __half* lnx_w,
+                        const __half* lnx_b, __half* yg, int M, int C, cudaStream_t st);
 
 namespace {
 
@@ -70,7 +85,18 @@ struct Carve {
 
 struct Work {
   __half *x, *x1, *xmix, *rkv, *ranks, *gbuf, *vfirst, *yg, *xk, *h, *xlast, *lnout;
+  float* chunk_rec;
+  int* chunk_cu;
 };
+
+// The chunk-parallel wkv pays off once sequences are long; one-token rows
+// (decode) use the fused per-token kernel. RWKV_B200_WKV=serial|chunked forces one.
+bool use_chunked_wkv(int M, int S) {
+  const char* e = getenv("RWKV_B200_WKV");
+  if (e && e[0] == 's') return false;
+  if (e && e[0] == 'c') return true;
+  return M >= 32 * S;
+}
 
 Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) {
   Carve c(base);
@@ -88,6 +114,8 @@ Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) 
   w.h = c.take<__half>(4 * MC);
   w.xlast = c.take<__half>((size_t)L * 2 * S * C);
   w.lnout = c.take<__half>((size_t)n_logits * C);
+  w.chunk_cu = c.take<int>((size_t)S + 1);
+  w.chunk_rec = c.take<float>(wkv_chunk_record_bytes(M, S, C / RWKV_HD) / sizeof(float));
   total = c.off;
   return w;
 }
@@ -165,6 +193,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const size_t CC = (size_t)C * C;
   const int ns = state->n_slots;
   const __half* emb = (const __half*)model->emb;
+  const bool chunked = use_chunked_wkv(M, S);
 
   for (int l = 0; l < L; ++l) {
     const rwkv7_layer& Lw = model->layers[l];
@@ -201,9 +230,17 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
     TRY(launch_gates(sem, w.ranks, (const __half*)Lw.w_lora_up, w.rkv, (const __half*)Lw.w0,
                      (const __half*)Lw.a0, (const __half*)Lw.v0, (const __half*)Lw.k_k,
                      (const __half*)Lw.k_a, w.vfirst, w.gbuf, M, C, l == 0, st));
-    TRY(launch_wkv_tokens(sem, w.rkv, w.gbuf, MC, (const __half*)Lw.r_k, (const __half*)Lw.lnx_w,
-                          (const __half*)Lw.lnx_b, st_rnn, b->cu_seqlens, b->slots, w.yg, S, H, C,
-                          st));
+    if (chunked) {
+      // gbuf planes: 0 w, 1 k, 2 v, 3 A (k_hat), 4 B; r from the rkv buffer
+      TRY(launch_wkv_chunked(w.rkv, w.gbuf, w.gbuf + MC, w.gbuf + 2 * MC, w.gbuf + 3 * MC,
+                             w.gbuf + 4 * MC, st_rnn, b->cu_seqlens, b->slots, w.xk, w.chunk_rec,
+                             w.chunk_cu, M, S, H, st));
+      TRY(launch_wkv_epilogue(sem, w.xk, w.rkv, w.gbuf, MC, (const __half*)Lw.r_k,
+                              (const __half*)Lw.lnx_w, (const __half*)Lw.lnx_b, w.yg, M, C, st));
+    } else
+      TRY(launch_wkv_tokens(sem, w.rkv, w.gbuf, MC, (const __half*)Lw.r_k,
+                            (const __half*)Lw.lnx_w, (const __half*)Lw.lnx_b, st_rnn,
+                            b->cu_seqlens, b->slots, w.yg, S, H, C, st));
     {
       rwkv7_gemm_problem p = {w.yg, Lw.w_o, w.x1, w.x, M, C, C, C, C, C};
       TRY(gemm_launch(&p, 1, RWKV_EPI_RESID, st));

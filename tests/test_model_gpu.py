@@ -11,10 +11,9 @@ from __future__ import annotations
 import pytest
 import torch
 
-from oracle.rwkv7_oracle import OracleState, OracleWeights, RWKV7Oracle
 from rwkv_tl_b200 import BatchedState, RWKV7B200, RWKV7Weight, State, make_rwkv7
-from rwkv_tl_b200.synth import CONFIG_0_1B, CONFIG_0_4B, CONFIG_TINY, synth_checkpoint
-from tests._util import assert_logits_close, assert_state_close, gpu_state_to_oracle
+from rwkv_tl_b200.synth import CONFIG_0_1B, CONFIG_0_4B, CONFIG_TINY, ModelConfig, synth_checkpoint
+from tests._util import OraclePair, assert_logits_close, assert_state_close, gpu_state_to_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -27,7 +26,7 @@ def _pair(cfg, seed):
         sd = synth_checkpoint(cfg, seed=seed)
         w = RWKV7Weight(sd, device="cuda")
         _CACHE.clear()
-        _CACHE[key] = (RWKV7B200(w), RWKV7Oracle(OracleWeights(sd, mode="fp16")))
+        _CACHE[key] = (RWKV7B200(w), OraclePair(sd))
     return _CACHE[key]
 
 
@@ -36,9 +35,23 @@ def _tokens(n, V, seed):
     return torch.randint(0, V, (n,), generator=g).tolist()
 
 
+def test_one_layer_strict_north_star_bar():
+    """A 1-layer 0.1B-width model sits above the fp16 noise floor: hold it to the
+    north star's absolute bar (max-abs 2e-2, rel-L2 1e-3, state rel 1e-3)."""
+    m, o = _pair(ModelConfig(n_layer=1, n_embd=768, vocab=4096), 2)
+    S, So = State(m.L, m.C, 64, device="cuda"), o.state()
+    toks = _tokens(24, 4096, 9)
+    lg, S = m.forward(torch.tensor(toks[:16], device="cuda"), S)
+    assert_logits_close(lg.float(), o.forward(toks[:16], So), "1-layer forward", strict=True)
+    for i, t in enumerate(toks[16:]):
+        lg, S = m.decode(torch.tensor([t], device="cuda"), S)
+        assert_logits_close(lg.float(), o.decode(t, So), f"1-layer decode {i}", strict=True)
+    assert_state_close(S, So, "1-layer", strict=True)
+
+
 def test_tiny_decode_per_token():
     m, o = _pair(CONFIG_TINY, 1)
-    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    S, So = State(m.L, m.C, 64, device="cuda"), o.state()
     for i, t in enumerate(_tokens(12, CONFIG_TINY.vocab, 0)):
         lg, S = m.decode(torch.tensor([t], device="cuda"), S)
         assert_logits_close(lg.float(), o.decode(t, So), f"step {i}")
@@ -48,7 +61,7 @@ def test_tiny_decode_per_token():
 def test_tiny_forward_prefill_then_decode():
     m, o = _pair(CONFIG_TINY, 1)
     toks = _tokens(33, CONFIG_TINY.vocab, 1)
-    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    S, So = State(m.L, m.C, 64, device="cuda"), o.state()
     lg, S = m.forward(torch.tensor(toks, device="cuda"), S)
     assert_logits_close(lg.float(), o.forward(toks, So), "forward")
     assert_state_close(S, So, "tiny forward")
@@ -62,8 +75,10 @@ def test_prefill_chunking_matches_single_call():
     m2 = RWKV7B200(m.w, max_rows=16)
     S2 = State(m.L, m.C, 64, device="cuda")
     m2.prefill(toks, S2)
+    # chunks of 16 rows take the per-token wkv, the single call the chunked one
     for a, b in zip(S1.tmix, S2.tmix):
-        assert torch.equal(a["rnn"], b["rnn"]) and torch.equal(a["x"], b["x"])
+        assert ((a["rnn"] - b["rnn"]).norm() / a["rnn"].norm()) < 1e-3
+        assert (a["x"].float() - b["x"].float()).abs().max() < 1e-2
 
 
 def test_cfg0_greedy_0p1b():
@@ -71,13 +86,13 @@ def test_cfg0_greedy_0p1b():
     m, o = _pair(CONFIG_0_1B, 0)
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, 65536, (8,), generator=g).tolist()
-    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    S, So = State(m.L, m.C, 64, device="cuda"), o.state()
     lg, S = m.forward(torch.tensor(prompt, device="cuda"), S)
     olg = o.forward(prompt, So)
     assert_logits_close(lg.float(), olg, "prompt")
     agree = 0
     for step in range(16):
-        tok = int(olg.argmax())
+        tok = int(olg[0].argmax())
         agree += int(lg.float().argmax()) == tok
         if step == 15:
             break
@@ -91,7 +106,7 @@ def test_cfg0_greedy_0p1b():
 def test_0p4b_prefill64_and_decode():
     m, o = _pair(CONFIG_0_4B, 0)
     toks = _tokens(64, 65536, 3)
-    S, So = State(m.L, m.C, 64, device="cuda"), OracleState(o.w.L, o.w.C)
+    S, So = State(m.L, m.C, 64, device="cuda"), o.state()
     lg, S = m.forward(torch.tensor(toks, device="cuda"), S)
     assert_logits_close(lg.float(), o.forward(toks, So), "0.4B forward")
     for i, t in enumerate(_tokens(3, 65536, 4)):
@@ -112,7 +127,7 @@ def test_decode_batch_random_states():
     toks = _tokens(B, CONFIG_TINY.vocab, 6)
     oracle_states = []
     for b in range(B):
-        So = OracleState(o.w.L, o.w.C)
+        So = o.state()
         gpu_state_to_oracle(bs[b], So)
         oracle_states.append(So)
     lg = m.decode_batch(torch.tensor(toks, device="cuda"), bs)
@@ -129,7 +144,7 @@ def test_prefill_batch_varlen_and_slots():
     slots = [5, 0, 3, 1]
     lg = m.forward_batch([torch.tensor(s) for s in seqs], bs, slots)
     for i, s in enumerate(seqs):
-        So = OracleState(o.w.L, o.w.C)
+        So = o.state()
         assert_logits_close(lg[i].float(), o.forward(s, So), f"seq {i}")
         assert_state_close(bs[slots[i]], So, f"seq {i}")
     # untouched slots stay zero
@@ -159,7 +174,7 @@ def test_foreign_state_layout_roundtrip():
     S = State(m.L, m.C, 64, device="cuda")
     for d in S.tmix:
         d["rnn"] = d["rnn"].clone()  # rebind: no longer aliases the blocks
-    So = OracleState(o.w.L, o.w.C)
+    So = o.state()
     for t in _tokens(4, CONFIG_TINY.vocab, 8):
         lg, S = m.decode(t, S)
         assert_logits_close(lg.float(), o.decode(t, So), "foreign")
@@ -175,3 +190,22 @@ def test_errors():
         m.forward(torch.zeros(2, 2, dtype=torch.long, device="cuda"), S)
     with pytest.raises(ValueError):
         make_rwkv7(torch.device("cuda"), backend="nope")
+
+
+@pytest.mark.parametrize("lens", [[70], [1, 33, 16, 100], [17, 5]])
+def test_chunked_wkv_matches_serial(monkeypatch, lens):
+    """The chunk-parallel wkv and the per-token wkv give the same model state (to the
+    fp32 noise that fp16 rounding amplifies through the layers: state rel 1e-3)."""
+    m, _ = _pair(CONFIG_TINY, 1)
+    seqs = [torch.tensor(_tokens(n, CONFIG_TINY.vocab, 20 + i)) for i, n in enumerate(lens)]
+    out = {}
+    for mode in ("serial", "chunked"):
+        monkeypatch.setenv("RWKV_B200_WKV", mode)
+        bs = BatchedState(m.L, m.C, len(lens), device="cuda")
+        m.prefill_batch(seqs, bs)
+        torch.cuda.synchronize()
+        out[mode] = bs
+    a, b = out["serial"], out["chunked"]
+    assert ((a.rnn - b.rnn).norm() / a.rnn.norm()) < 1e-3
+    assert (a.tmix_x.float() - b.tmix_x.float()).abs().max() < 1e-2
+    assert (a.cmix_x.float() - b.cmix_x.float()).abs().max() < 1e-2

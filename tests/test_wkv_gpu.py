@@ -84,3 +84,39 @@ def test_dplr_rejects_bad_args():
     rc = lib.rwkv7_dplr_step(None, None, None, None, None, None, None, None, 1, 16, None)
     assert rc == _lib.RWKV_ERR_ARG
     assert b"rwkv7_dplr_step" in lib.rwkv_b200_last_error()
+
+
+def _batched_ref(S0, r, w, k, v, A, Bv):
+    """Serial fp32 recurrence, batched over sequences: inputs [B, T, H, 64]."""
+    S = S0.clone()
+    ys = torch.empty(r.shape, dtype=torch.float32)
+    f = lambda t: t.float()  # noqa: E731
+    r, w, k, v, A, Bv = map(f, (r, w, k, v, A, Bv))
+    for t in range(r.shape[1]):
+        sa = torch.einsum("bhvk,bhk->bhv", S, A[:, t])
+        S = S * w[:, t, :, None, :] + sa[..., None] * Bv[:, t, :, None, :] + v[:, t, :, :, None] * k[:, t, :, None, :]
+        ys[:, t] = torch.einsum("bhvk,bhk->bhv", S, r[:, t])
+    return ys, S
+
+
+@pytest.mark.parametrize("B,T", [(1, 64), (8, 64), (1, 1024), (8, 1024), (64, 64), (1, 4096),
+                                 (3, 37)])
+def test_dplr_chunked_config1(B, T):
+    """BASELINE config 1 sweep (H=16) through the chunk-parallel kernel."""
+    from rwkv_tl_b200 import _lib
+
+    lib = _lib.load()
+    H = 16
+    r, w, k, v, A, Bv, S0 = _inputs(B, T, H, seed=B * 10000 + T)
+    yref, Sref = _batched_ref(S0, r, w, k, v, A, Bv)
+    dev = [t.contiguous().cuda() for t in (r, w, k, v, A, Bv)]
+    S = S0.cuda().contiguous()
+    y = torch.empty(B, T, H, 64, dtype=torch.float16, device="cuda")
+    nbytes = lib.rwkv7_dplr_chunked_workspace_bytes(B, T, H)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    _lib.check(lib.rwkv7_dplr_chunked(S.data_ptr(), *[t.data_ptr() for t in dev], y.data_ptr(),
+                                      B, T, H, ws.data_ptr(), nbytes,
+                                      torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert rel_l2(S, Sref) < 1e-4
+    assert rel_l2(y.float(), yref) < 1e-3
