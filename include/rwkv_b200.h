@@ -116,6 +116,10 @@ int rwkv_b200_abi_version(void);
 /* Number of kernel launches this library has issued from the host so far (a
  * captured CUDA graph replays its kernels without passing through here). */
 unsigned long long rwkv_b200_launch_count(void);
+/* Nonzero if, since the last call, a kernel on the current device gave up on a
+ * bounded wait (a pipeline barrier that never completed) instead of spinning
+ * forever; reading clears it. Synchronous (reads device memory). */
+int rwkv_b200_device_error(void);
 
 /* wkv7 DPLR step, batched over n_seq independent sequences (T = 1):
  *   sa[v] = sum_j S[v,j] a[j];  S[v,k] = S[v,k] w[k] + sa[v] b[k] + v[v] k[k];

@@ -18,6 +18,7 @@ EXPORTED = (
     "rwkv_b200_last_error",
     "rwkv_b200_abi_version",
     "rwkv_b200_launch_count",
+    "rwkv_b200_device_error",
     "rwkv7_dplr_step",
     "rwkv7_dplr_seq",
     "rwkv7_dplr_chunked_workspace_bytes",
@@ -97,6 +98,7 @@ def load() -> C.CDLL:
     lib.rwkv_b200_last_error.restype = C.c_char_p
     lib.rwkv_b200_abi_version.restype = C.c_int
     lib.rwkv_b200_launch_count.restype = C.c_ulonglong
+    lib.rwkv_b200_device_error.restype = C.c_int
     for name in ("rwkv7_dplr_step", "rwkv7_dplr_seq"):
         f = getattr(lib, name)
         f.restype = C.c_int

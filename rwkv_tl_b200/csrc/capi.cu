@@ -35,6 +35,9 @@ int rwkv_check_launch(const char* what) {
 
 extern "C" const char* rwkv_b200_last_error(void) { return g_err; }
 extern "C" int rwkv_b200_abi_version(void) { return RWKV_B200_ABI_VERSION; }
+int gemm_tc_timeout_flag();
+extern "C" int rwkv_b200_device_error(void) { return gemm_tc_timeout_flag(); }
+
 extern "C" unsigned long long rwkv_b200_launch_count(void) {
   return __atomic_load_n(&g_launches, __ATOMIC_RELAXED);
 }
@@ -59,7 +62,8 @@ int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t pl
                       const __half* r_k, const __half* lnx_w, const __half* lnx_b, float* rnn,
                       const int* cu, const int* slots, __half* yg, int n_seqs, int H, int C,
                       cudaStream_t st);
-int gemm_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStream_t st);
+int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
+                   size_t ws_floats, cudaStream_t st);
 size_t wkv_chunk_record_bytes(int M, int S, int H);
 int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
                        const __half* a, const __half* b, float* rnn, const int* cu,
@@ -87,7 +91,12 @@ struct Work {
   __half *x, *x1, *xmix, *rkv, *ranks, *gbuf, *vfirst, *yg, *xk, *h, *xlast, *lnout;
   float* chunk_rec;
   int* chunk_cu;
+  float* splitk;  // zeroed fp32 split-K scratch for small-M GEMMs
+  size_t splitk_floats;
 };
+
+// split-K scratch only pays for small token batches
+size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)4 * M * C : 0; }
 
 // The chunk-parallel wkv pays off once sequences are long; one-token rows
 // (decode) use the fused per-token kernel. RWKV_B200_WKV=serial|chunked forces one.
@@ -116,6 +125,8 @@ Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) 
   w.lnout = c.take<__half>((size_t)n_logits * C);
   w.chunk_cu = c.take<int>((size_t)S + 1);
   w.chunk_rec = c.take<float>(wkv_chunk_record_bytes(M, S, C / RWKV_HD) / sizeof(float));
+  w.splitk_floats = splitk_floats(M, C);
+  w.splitk = w.splitk_floats ? c.take<float>(w.splitk_floats) : nullptr;
   total = c.off;
   return w;
 }
@@ -194,6 +205,9 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const int ns = state->n_slots;
   const __half* emb = (const __half*)model->emb;
   const bool chunked = use_chunked_wkv(M, S);
+  if (w.splitk &&
+      cudaMemsetAsync(w.splitk, 0, w.splitk_floats * sizeof(float), st) != cudaSuccess)
+    return rwkv_check_launch("splitk memset");
 
   for (int l = 0; l < L; ++l) {
     const rwkv7_layer& Lw = model->layers[l];
@@ -215,7 +229,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
           {w.xmix + 0 * MC, wrkv + 0 * CC, w.rkv + 0 * MC, nullptr, M, C, C, C, C, C},
           {w.xmix + 2 * MC, wrkv + 1 * CC, w.rkv + 1 * MC, nullptr, M, C, C, C, C, C},
           {w.xmix + 3 * MC, wrkv + 2 * CC, w.rkv + 2 * MC, nullptr, M, C, C, C, C, C}};
-      TRY(gemm_launch(p, 3, RWKV_EPI_STORE, st));
+      TRY(gemm_launch_ws(p, 3, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
     }
     {
       // LoRA down-projections into ranks [M, 288] = v(32) | w(64) | a(64) | g(128)
@@ -225,7 +239,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
           {w.xmix + 1 * MC, wdn + 32 * C, w.ranks + 32, nullptr, M, 64, C, C, C, R},
           {w.xmix + 4 * MC, wdn + 96 * C, w.ranks + 96, nullptr, M, 64, C, C, C, R},
           {w.xmix + 5 * MC, wdn + 160 * C, w.ranks + 160, nullptr, M, 128, C, C, C, R}};
-      TRY(gemm_launch(p, 4, RWKV_EPI_STORE, st));
+      TRY(gemm_launch_ws(p, 4, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
     }
     TRY(launch_gates(sem, w.ranks, (const __half*)Lw.w_lora_up, w.rkv, (const __half*)Lw.w0,
                      (const __half*)Lw.a0, (const __half*)Lw.v0, (const __half*)Lw.k_k,
@@ -243,7 +257,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
                             b->cu_seqlens, b->slots, w.yg, S, H, C, st));
     {
       rwkv7_gemm_problem p = {w.yg, Lw.w_o, w.x1, w.x, M, C, C, C, C, C};
-      TRY(gemm_launch(&p, 1, RWKV_EPI_RESID, st));
+      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RESID, w.splitk, w.splitk_floats, st));
     }
     // ---- CMIX ----
     TRY(launch_cmix_rows(sem, w.x1, (const __half*)Lw.ln2_w, (const __half*)Lw.ln2_b,
@@ -251,11 +265,11 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
                          w.xk, xl_c, M, C, st));
     {
       rwkv7_gemm_problem p = {w.xk, Lw.w_fk, w.h, nullptr, M, 4 * C, C, C, C, 4 * C};
-      TRY(gemm_launch(&p, 1, RWKV_EPI_RELUSQ, st));
+      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RELUSQ, w.splitk, w.splitk_floats, st));
     }
     {
       rwkv7_gemm_problem p = {w.h, Lw.w_fv, w.x, w.x1, M, C, 4 * C, 4 * C, 4 * C, C};
-      TRY(gemm_launch(&p, 1, RWKV_EPI_RESID, st));
+      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RESID, w.splitk, w.splitk_floats, st));
     }
   }
   if (b->n_logits) {
@@ -263,7 +277,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
                        (const __half*)model->lnout_b, w.lnout, b->n_logits, C, st));
     rwkv7_gemm_problem p = {w.lnout, model->head, b->logits, nullptr, b->n_logits, model->vocab,
                             C, C, C, model->vocab};
-    TRY(gemm_launch(&p, 1, RWKV_EPI_STORE, st));
+    TRY(gemm_launch_ws(&p, 1, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
   }
   TRY(launch_scatter_state_x(w.xlast, (__half*)state->tmix_x, (__half*)state->cmix_x, b->slots, S,
                              L, ns, C, st));

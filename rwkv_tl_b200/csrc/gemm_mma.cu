@@ -5,6 +5,8 @@
 // prefill / batched-decode problems. Tile 128x128x32, 4-stage cp.async
 // pipeline, 8 warps (2 x 4, warp tile 64 x 32), XOR-swizzled shared memory
 // read with ldmatrix.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace {
@@ -219,8 +221,36 @@ int gemm_mma_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStre
   return RWKV_ERR_ARG;
 }
 
+bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n);
+int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
+                   cudaStream_t st);
+
+// Kernel choice by shape: the tcgen05 kernel when every problem has K % 64 == 0
+// (all model projections), else the mma.sync kernel. Small output grids are
+// split along K (fp32 partials in `ws`, which must be zero and holds
+// ws_floats floats) to fill the 148 SMs. RWKV_B200_GEMM=mma|tc forces a kernel.
+int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
+                   size_t ws_floats, cudaStream_t st) {
+  const char* e = getenv("RWKV_B200_GEMM");
+  const bool force_mma = e && e[0] == 'm';
+  if (force_mma || !gemm_tc_eligible(problems, n)) return gemm_mma_launch(problems, n, epi, st);
+  int tiles = 0, min_kb = 1 << 30;
+  size_t need = 0;
+  for (int i = 0; i < n; ++i) {
+    tiles += ((problems[i].M + 127) / 128) * ((problems[i].N + 127) / 128);
+    min_kb = min(min_kb, problems[i].K / 64);
+    need += (size_t)problems[i].M * problems[i].N;
+  }
+  int splits = 1;
+  if (ws && need <= ws_floats && tiles < 120) {
+    splits = min(min_kb / 2, (148 + tiles - 1) / tiles);
+    splits = max(splits, 1);
+  }
+  return gemm_tc_launch(problems, n, epi, splits, ws, st);
+}
+
 int gemm_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStream_t st) {
-  return gemm_mma_launch(problems, n, epi, st);
+  return gemm_launch_ws(problems, n, epi, nullptr, 0, st);
 }
 
 extern "C" int rwkv7_gemm_f16(const rwkv7_gemm_problem* problems, int n_problems, int epilogue,

@@ -1,0 +1,473 @@
+// Grouped fp16 GEMM on the 5th-generation tensor cores (tcgen05 + TMA + TMEM).
+//
+// C[M, N] = epi(A[M, K] @ B[N, K]^T): A and B are both K-major (row-major with
+// the reduction dim contiguous), which is the layout every projection here
+// has (weights keep the checkpoint's [out, in] orientation).
+//
+// One CTA computes a 128 x BN output tile (or a K-slice of it, split-K):
+//   warp 0      TMA producer: 128B-swizzled 128x64 (A) and BNx64 (B) fp16 tiles
+//               into a STAGES-deep shared-memory ring (mbarrier full/empty);
+//   warp 1      allocates BN TMEM columns, one elected thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) x 4 per
+//               stage and tcgen05.commit's the stage back to the producer;
+//   warps 2-5   epilogue: tcgen05.ld 32x32b (each warp its 32-lane TMEM
+//               quadrant = 32 output rows), fused epilogue, fp16 stores; with
+//               split-K they add fp32 partials into a workspace instead and
+//               k_tc_fixup applies the epilogue.
+// No TMA multicast is used anywhere (the kernels also run in multi-GPU jobs).
+// Every mbarrier wait is bounded: on timeout the CTA records an error flag
+// and leaves its loops instead of spinning forever.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BK = 64, STAGES = 6;
+constexpr int NTHREADS = 192;
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+
+__device__ int g_tc_timeout = 0;
+
+struct TcProblem {
+  void* C;
+  const void* R;
+  float* ws;  // split-K accumulator [M, N] (fp32, zero on entry), or null
+  int M, N, K, ldc;
+};
+
+struct TcParams {
+  CUtensorMap ta[4];
+  CUtensorMap tb[4];
+  TcProblem p[4];
+  int n_problems;
+  int splits;
+};
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; false (and the global error flag set) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicExch(&g_tc_timeout, 1);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(saddr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// K-major operand tile with 128-byte swizzle: rows of 64 fp16 (128 B), 8-row
+// swizzle atoms 1024 B apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
+  const uint64_t addr = saddr(tile);
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: fp16 A/B, fp32 D, both K-major, M = 128, N = BN.
+template <int BN>
+__device__ __forceinline__ uint32_t instr_desc() {
+  return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   saddr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15},"
+      " [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int EPI>
+__device__ __forceinline__ __half2 epi2(float c0, float c1, const __half* R, size_t o) {
+  if (EPI == RWKV_EPI_STORE) return __floats2half2_rn(c0, c1);
+  if (EPI == RWKV_EPI_RESID) {
+    const float2 r = __half22float2(*reinterpret_cast<const __half2*>(R + o));
+    return __floats2half2_rn(r.x + r16(c0), r.y + r16(c1));
+  }
+  const float h0 = fmaxf(r16(c0), 0.f), h1 = fmaxf(r16(c1), 0.f);
+  return __floats2half2_rn(h0 * h0, h1 * h1);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__ TcParams prm) {
+  extern __shared__ unsigned char smem_raw[];
+  const int g = blockIdx.z % prm.n_problems;
+  const int split = blockIdx.z / prm.n_problems;
+  const TcProblem& P = prm.p[g];
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  if (n0 >= P.N || m0 >= P.M) return;
+  const int KB = P.K / BK;
+  const int kb_per = (KB + prm.splits - 1) / prm.splits;
+  const int kb0 = split * kb_per, kb1 = min(KB, kb0 + kb_per);
+  if (kb0 >= kb1) return;
+
+  // shared memory: [A stages][B stages] (1024-aligned) | barriers | tmem address
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+  unsigned char* sA = base;
+  unsigned char* sB = base + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(tmem_slot)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int issued = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int s = issued % STAGES;
+        const uint32_t round = issued / STAGES;
+        if (!mbar_wait(&empty[s], (round & 1) ^ 1)) break;
+        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+        tma_load_2d(sA + s * A_BYTES, &prm.ta[g], &full[s], kb * BK, m0);
+        tma_load_2d(sB + s * B_BYTES, &prm.tb[g], &full[s], kb * BK, n0);
+        ++issued;
+      }
+      // drain: never leave the CTA while copies may still land in shared memory
+      for (int i = max(0, issued - STAGES); i < issued; ++i)
+        mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = instr_desc<BN>();
+      int it = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&full[s], (it / STAGES) & 1)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t ad = smem_desc_sw128(sA + s * A_BYTES);
+        const uint64_t bd = smem_desc_sw128(sB + s * B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // +32 bytes per K=16 step inside the 128-byte swizzle atom (>> 4 in the descriptor)
+          umma_f16(tmem, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), idesc,
+                   (kb > kb0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(tmem_full);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const bool ok = mbar_wait(tmem_full, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int row = m0 + quad * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    __half* C = static_cast<__half*>(P.C);
+    const __half* R = static_cast<const __half*>(P.R);
+    const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
+    if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(trow + c0, v);  // all lanes execute (sync.aligned)
+        const int col = n0 + c0;
+        if (row < P.M && col < P.N) {
+          if (P.ws) {
+            float* W = P.ws + (size_t)row * P.N + col;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (col + i < P.N) atomicAdd(W + i, v[i]);
+          } else {
+            const size_t o = (size_t)row * P.ldc + col;
+            if (col + 16 <= P.N) {
+              uint4 pk[2];
+              __half2* h2 = reinterpret_cast<__half2*>(pk);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) h2[i] = epi2<EPI>(v[2 * i], v[2 * i + 1], R, o + 2 * i);
+              if (vec) {
+                reinterpret_cast<uint4*>(C + o)[0] = pk[0];
+                reinterpret_cast<uint4*>(C + o)[1] = pk[1];
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) reinterpret_cast<__half2*>(C + o)[i] = h2[i];
+              }
+            } else {
+              for (int i = 0; i + 1 < 16 && col + i < P.N; i += 2)
+                *reinterpret_cast<__half2*>(C + o + i) = epi2<EPI>(v[i], v[i + 1], R, o + i);
+            }
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
+// Split-K fixup: C = epi(ws), then ws = 0 for the next use. grid = M, block = 256.
+template <int EPI>
+__global__ void k_tc_fixup(float* __restrict__ ws, __half* __restrict__ C,
+                           const __half* __restrict__ R, int N, int ldc) {
+  const int m = blockIdx.x;
+  for (int c = threadIdx.x * 2; c < N; c += blockDim.x * 2) {
+    float* w = ws + (size_t)m * N + c;
+    const float2 acc = *reinterpret_cast<float2*>(w);
+    *reinterpret_cast<float2*>(w) = make_float2(0.f, 0.f);
+    const size_t o = (size_t)m * ldc + c;
+    *reinterpret_cast<__half2*>(C + o) = epi2<EPI>(acc.x, acc.y, R, o);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps (cached), launch
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  int rows, cols, ld, box_rows, dev;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld &&
+           box_rows == o.box_rows && dev == o.dev;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = reinterpret_cast<size_t>(k.ptr);
+    h ^= (size_t)k.rows * 0x9E3779B97F4A7C15ull + (size_t)k.cols * 0xC2B2AE3D27D4EB4Full +
+         (size_t)k.ld * 0x165667B19E3779F9ull + (size_t)k.box_rows * 31 + (size_t)k.dev * 7;
+    return h;
+  }
+};
+
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// 2-D fp16 row-major [rows, cols] (row stride ld elements), box = [box_rows, 64], 128B swizzle.
+int make_map(CUtensorMap* out, const void* ptr, int rows, int cols, int ld, int box_rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const MapKey key{ptr, rows, cols, ld, box_rows, dev};
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return RWKV_OK;
+    }
+  }
+  auto enc = get_encode();
+  if (!enc) {
+    rwkv_set_error("gemm_tc: cuTensorMapEncodeTiled unavailable");
+    return RWKV_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    rwkv_set_error("gemm_tc: cuTensorMapEncodeTiled failed (%d) rows=%d cols=%d ld=%d", (int)r,
+                   rows, cols, ld);
+    return RWKV_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(key, *out);
+  return RWKV_OK;
+}
+
+template <int BN>
+constexpr int smem_bytes() {
+  return 1024 + STAGES * (BM * BK * 2 + BN * BK * 2) + (2 * STAGES + 1) * 8 + 16;
+}
+
+template <int BN, int EPI>
+int launch_tc(const TcParams& prm, dim3 grid, cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool done[64] = {};
+  if (dev < 64 && !done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smem_bytes<BN>());
+    if (e != cudaSuccess) {
+      rwkv_set_error("gemm_tc: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return RWKV_ERR_CUDA;
+    }
+    done[dev] = true;
+  }
+  k_gemm_tc<BN, EPI><<<grid, NTHREADS, smem_bytes<BN>(), st>>>(prm);
+  return rwkv_check_launch("gemm_tc");
+}
+
+}  // namespace
+
+// True when every problem fits the tcgen05 path (K multiple of 64, aligned operands).
+bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n) {
+  for (int i = 0; i < n; ++i) {
+    if (p[i].K % BK || p[i].lda % 8 || p[i].ldb % 8 || p[i].M <= 0 || p[i].N <= 0) return false;
+    if ((reinterpret_cast<uintptr_t>(p[i].A) | reinterpret_cast<uintptr_t>(p[i].B)) & 15)
+      return false;
+    if ((reinterpret_cast<uintptr_t>(p[i].C) | reinterpret_cast<uintptr_t>(p[i].R)) & 3) return false;
+  }
+  return true;
+}
+
+// splits > 1 needs `ws` = zeroed fp32 scratch of sum_i M_i * N_i floats (re-zeroed on exit).
+int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
+                   cudaStream_t st) {
+  TcParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.n_problems = n;
+  prm.splits = splits;
+  constexpr int BN = 128;
+  int gx = 0, gy = 0;
+  size_t ws_off = 0;
+  for (int i = 0; i < n; ++i) {
+    int rc = make_map(&prm.ta[i], p[i].A, p[i].M, p[i].K, p[i].lda, BM);
+    if (rc) return rc;
+    rc = make_map(&prm.tb[i], p[i].B, p[i].N, p[i].K, p[i].ldb, BN);
+    if (rc) return rc;
+    prm.p[i].C = p[i].C;
+    prm.p[i].R = p[i].R;
+    prm.p[i].M = p[i].M;
+    prm.p[i].N = p[i].N;
+    prm.p[i].K = p[i].K;
+    prm.p[i].ldc = p[i].ldc;
+    prm.p[i].ws = splits > 1 ? ws + ws_off : nullptr;
+    ws_off += (size_t)p[i].M * p[i].N;
+    gx = max(gx, (p[i].N + BN - 1) / BN);
+    gy = max(gy, (p[i].M + BM - 1) / BM);
+  }
+  dim3 grid(gx, gy, n * splits);
+  int rc;
+  switch (epi) {
+    case RWKV_EPI_STORE: rc = launch_tc<BN, RWKV_EPI_STORE>(prm, grid, st); break;
+    case RWKV_EPI_RESID: rc = launch_tc<BN, RWKV_EPI_RESID>(prm, grid, st); break;
+    default: rc = launch_tc<BN, RWKV_EPI_RELUSQ>(prm, grid, st); break;
+  }
+  if (rc || splits == 1) return rc;
+  for (int i = 0; i < n; ++i) {
+    __half* C = static_cast<__half*>(p[i].C);
+    const __half* R = static_cast<const __half*>(p[i].R);
+    switch (epi) {
+      case RWKV_EPI_STORE:
+        k_tc_fixup<RWKV_EPI_STORE><<<p[i].M, 256, 0, st>>>(prm.p[i].ws, C, R, p[i].N, p[i].ldc);
+        break;
+      case RWKV_EPI_RESID:
+        k_tc_fixup<RWKV_EPI_RESID><<<p[i].M, 256, 0, st>>>(prm.p[i].ws, C, R, p[i].N, p[i].ldc);
+        break;
+      default:
+        k_tc_fixup<RWKV_EPI_RELUSQ><<<p[i].M, 256, 0, st>>>(prm.p[i].ws, C, R, p[i].N, p[i].ldc);
+        break;
+    }
+    if ((rc = rwkv_check_launch("gemm_tc_fixup"))) return rc;
+  }
+  return RWKV_OK;
+}
+
+// Host read of the device timeout flag (cleared on read); nonzero means a bounded wait gave up.
+int gemm_tc_timeout_flag() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_timeout, sizeof(int));
+  if (v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_tc_timeout, &z, sizeof(int));
+  }
+  return v;
+}

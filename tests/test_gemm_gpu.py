@@ -8,6 +8,17 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["tc", "mma"], autouse=True)
+def gemm_kernel(request, monkeypatch):
+    """Run every case on the tcgen05 kernel and on the mma.sync kernel."""
+    monkeypatch.setenv("RWKV_B200_GEMM", request.param)
+    yield request.param
+    from rwkv_tl_b200 import _lib
+
+    torch.cuda.synchronize()
+    assert _lib.load().rwkv_b200_device_error() == 0
+
+
 def _run(problems, epi):
     from rwkv_tl_b200 import _lib
 
@@ -24,7 +35,7 @@ def _run(problems, epi):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 3072, 1024), (7, 288, 1024), (130, 1024, 4096),
-                                   (256, 65536, 1024), (4096, 4096, 1024), (33, 32, 32)])
+                                   (256, 65536, 1024), (4096, 4096, 1024), (33, 32, 64), (300, 1000, 128)])
 def test_gemm_store(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
     A = torch.randn(M, K, device="cuda", generator=g).half()
