@@ -143,6 +143,19 @@ int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const void* k, con
                        const void* a, const void* b, void* y, int n_seq, int T, int H,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* rwkv7_dplr_chunked for callers that cannot allocate device memory (a frozen
+ * memory pool, a host framework that only hands out input/output buffers):
+ * no workspace argument, no allocation. Its scratch is a fixed 16 MiB device
+ * array inside this library, so it accepts only problems whose
+ * rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H) is at most 16 MiB and
+ * returns RWKV_ERR_SPACE otherwise. The first call on a device looks up the
+ * array's address (do it before any stream capture). All calls share the one
+ * array: calls that overlap on the GPU (different streams) race. No
+ * counterpart in the reference. */
+int rwkv7_dplr_chunked_noalloc(void* S, const void* r, const void* w, const void* k,
+                               const void* v, const void* a, const void* b, void* y, int n_seq,
+                               int T, int H, void* stream);
+
 /* Grouped fp16 GEMM, up to 4 independent problems in one launch:
  *   C_g[M_g, N_g] = epi( A_g[M_g, K_g] @ B_g[N_g, K_g]^T )
  * A row-major (lda), B row-major [N, K] (ldb), C/R row-major (ldc). K_g must be

@@ -17,6 +17,8 @@
 // (chunk, head); k_chunk_scan then walks the chunks of each sequence in order
 // with the fp32 state of 8 rows in registers (one warp per row). All math is
 // fp32; exponents stay within one chunk (|G| <= 16 * 0.6066), so no overflow.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -406,4 +408,64 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
   return launch_wkv_chunked((const __half*)r, (const __half*)w, (const __half*)k,
                             (const __half*)v, (const __half*)a, (const __half*)b, (float*)S, cu,
                             nullptr, (__half*)y, rec, chunk_cu, n_seq * T, n_seq, H, st);
+}
+
+// ---------------------------------------------------------------------------
+// rwkv7_dplr_chunked without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// recurrence: code running inside an allocator-free region (a memory pool
+// that must not grow, a host framework that owns all device allocations and
+// only hands out input/output buffers, a plugin loaded into a process whose
+// allocator is not reachable from this library). For them the scratch lives
+// in this file-scope array instead: every GPU that loads the library holds
+// these 16 MiB until the process exits. In host code `g_noalloc_scratch` is
+// only a host-side stand-in for the symbol, never a device address; the device
+// address comes from cudaGetSymbolAddress, once per device, on that device's
+// first call (make that first call before any stream capture).
+namespace {
+constexpr size_t NOALLOC_BYTES = (size_t)16 << 20;
+}
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {};
+
+extern "C" int rwkv7_dplr_chunked_noalloc(void* S, const void* r, const void* w, const void* k,
+                                          const void* v, const void* a, const void* b, void* y,
+                                          int n_seq, int T, int H, void* stream) {
+  if (n_seq <= 0 || T <= 0 || H <= 0) {
+    rwkv_set_error("rwkv7_dplr_chunked_noalloc: bad size (n_seq=%d, T=%d, H=%d)", n_seq, T, H);
+    return RWKV_ERR_ARG;
+  }
+  const size_t need = rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H);
+  if (need > NOALLOC_BYTES) {
+    rwkv_set_error(
+        "rwkv7_dplr_chunked_noalloc: n_seq=%d T=%d H=%d needs %zu bytes of scratch, more than the "
+        "built-in %zu; use rwkv7_dplr_chunked with a workspace",
+        n_seq, T, H, need, NOALLOC_BYTES);
+    return RWKV_ERR_SPACE;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    rwkv_set_error("rwkv7_dplr_chunked_noalloc: no usable current device");
+    return RWKV_ERR_CUDA;
+  }
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      cudaError_t e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_scratch);
+      if (e != cudaSuccess) {
+        g_noalloc_ptr[dev] = nullptr;
+        rwkv_set_error("rwkv7_dplr_chunked_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+        return RWKV_ERR_CUDA;
+      }
+    }
+    ptr = g_noalloc_ptr[dev];
+  }
+  // Nothing in the scratch has to start at zero: the sequence offsets, the
+  // chunk table and every chunk record read later are written first by this call.
+  return rwkv7_dplr_chunked(S, r, w, k, v, a, b, y, n_seq, T, H, ptr, NOALLOC_BYTES, stream);
 }
