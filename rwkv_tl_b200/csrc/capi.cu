@@ -91,12 +91,12 @@ struct Work {
   __half *x, *x1, *xmix, *rkv, *ranks, *gbuf, *vfirst, *yg, *xk, *h, *xlast, *lnout;
   float* chunk_rec;
   int* chunk_cu;
-  float* splitk;  // zeroed fp32 split-K scratch for small-M GEMMs
+  float* splitk;       // split-K partial tiles for small-M GEMMs
   size_t splitk_floats;
 };
 
-// split-K scratch only pays for small token batches
-size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)4 * M * C : 0; }
+// split-K only pays for small token batches
+size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)16 * M * C : 0; }
 
 // The chunk-parallel wkv pays off once sequences are long; one-token rows
 // (decode) use the fused per-token kernel. RWKV_B200_WKV=serial|chunked forces one.
@@ -205,9 +205,6 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const int ns = state->n_slots;
   const __half* emb = (const __half*)model->emb;
   const bool chunked = use_chunked_wkv(M, S);
-  if (w.splitk &&
-      cudaMemsetAsync(w.splitk, 0, w.splitk_floats * sizeof(float), st) != cudaSuccess)
-    return rwkv_check_launch("splitk memset");
 
   for (int l = 0; l < L; ++l) {
     const rwkv7_layer& Lw = model->layers[l];

@@ -227,25 +227,33 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, floa
 
 // Kernel choice by shape: the tcgen05 kernel when every problem has K % 64 == 0
 // (all model projections), else the mma.sync kernel. Small output grids are
-// split along K (fp32 partials in `ws`, which must be zero and holds
-// ws_floats floats) to fill the 148 SMs. RWKV_B200_GEMM=mma|tc forces a kernel.
+// split along K to fill the 148 SMs (at least 4 K-blocks per slice): `ws`
+// (ws_floats floats) takes the fp32 partial tiles, reduced by a second kernel.
+// RWKV_B200_GEMM=mma|tc forces a kernel.
 int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
                    size_t ws_floats, cudaStream_t st) {
   const char* e = getenv("RWKV_B200_GEMM");
   const bool force_mma = e && e[0] == 'm';
   if (force_mma || !gemm_tc_eligible(problems, n)) return gemm_mma_launch(problems, n, epi, st);
-  int tiles = 0, min_kb = 1 << 30;
-  size_t need = 0;
+  int tiles = 0, min_kb = 1 << 30, gx = 0, gy = 0;
+  size_t mn = 0;
   for (int i = 0; i < n; ++i) {
-    tiles += ((problems[i].M + 127) / 128) * ((problems[i].N + 127) / 128);
+    const int tx = (problems[i].N + 127) / 128, ty = (problems[i].M + 127) / 128;
+    tiles += tx * ty;
+    gx = max(gx, tx);
+    gy = max(gy, ty);
     min_kb = min(min_kb, problems[i].K / 64);
-    need += (size_t)problems[i].M * problems[i].N;
+    mn += (size_t)problems[i].M * problems[i].N;
   }
   int splits = 1;
-  if (ws && need <= ws_floats && tiles < 120) {
-    splits = min(min_kb / 2, (148 + tiles - 1) / tiles);
-    splits = max(splits, 1);
+  bool n4 = true;
+  for (int i = 0; i < n; ++i) n4 = n4 && (problems[i].N % 4 == 0) && (problems[i].ldc % 2 == 0);
+  if (ws && n4 && tiles < 148) {
+    splits = max(1, min(min_kb / 4, (2 * 148 + tiles - 1) / tiles));
+    while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
   }
+  (void)gx;
+  (void)gy;
   return gemm_tc_launch(problems, n, epi, splits, ws, st);
 }
 

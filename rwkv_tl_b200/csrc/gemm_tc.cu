@@ -12,8 +12,9 @@
 //               stage and tcgen05.commit's the stage back to the producer;
 //   warps 2-5   epilogue: tcgen05.ld 32x32b (each warp its 32-lane TMEM
 //               quadrant = 32 output rows), fused epilogue, fp16 stores; with
-//               split-K they add fp32 partials into a workspace instead and
-//               k_tc_fixup applies the epilogue.
+//               split-K each CTA parks its fp32 partial tile and
+//               k_splitk_reduce sums the slices in split order (deterministic)
+//               and applies the epilogue.
 // No TMA multicast is used anywhere (the kernels also run in multi-GPU jobs).
 // Every mbarrier wait is bounded: on timeout the CTA records an error flag
 // and leaves its loops instead of spinning forever.
@@ -28,7 +29,7 @@
 
 namespace {
 
-constexpr int BM = 128, BK = 64, STAGES = 6;
+constexpr int BM = 128, BK = 64, STAGES = 3;  // 3 stages: two CTAs share an SM
 constexpr int NTHREADS = 192;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 
@@ -37,7 +38,7 @@ __device__ int g_tc_timeout = 0;
 struct TcProblem {
   void* C;
   const void* R;
-  float* ws;  // split-K accumulator [M, N] (fp32, zero on entry), or null
+  float* ws;     // split-K partial tiles [splits][M][N] fp32, or null
   int M, N, K, ldc;
 };
 
@@ -151,8 +152,31 @@ __device__ __forceinline__ __half2 epi2(float c0, float c1, const __half* R, siz
   return __floats2half2_rn(h0 * h0, h1 * h1);
 }
 
+// Apply the epilogue to 16 consecutive columns of one output row and store fp16.
+template <int EPI>
+__device__ __forceinline__ void store16(const float (&v)[16], __half* C, const __half* R, int row,
+                                        int col, int N, int ldc, bool vec) {
+  const size_t o = (size_t)row * ldc + col;
+  if (col + 16 <= N) {
+    uint4 pk[2];
+    __half2* h2 = reinterpret_cast<__half2*>(pk);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h2[i] = epi2<EPI>(v[2 * i], v[2 * i + 1], R, o + 2 * i);
+    if (vec) {
+      reinterpret_cast<uint4*>(C + o)[0] = pk[0];
+      reinterpret_cast<uint4*>(C + o)[1] = pk[1];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) reinterpret_cast<__half2*>(C + o)[i] = h2[i];
+    }
+  } else {
+    for (int i = 0; i + 1 < 16 && col + i < N; i += 2)
+      *reinterpret_cast<__half2*>(C + o + i) = epi2<EPI>(v[i], v[i + 1], R, o + i);
+  }
+}
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__ TcParams prm) {
+__global__ void __launch_bounds__(NTHREADS, 2) k_gemm_tc(const __grid_constant__ TcParams prm) {
   extern __shared__ unsigned char smem_raw[];
   const int g = blockIdx.z % prm.n_problems;
   const int split = blockIdx.z / prm.n_problems;
@@ -162,7 +186,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
   const int KB = P.K / BK;
   const int kb_per = (KB + prm.splits - 1) / prm.splits;
   const int kb0 = split * kb_per, kb1 = min(KB, kb0 + kb_per);
-  if (kb0 >= kb1) return;
+  // a K-slice past the end still writes its (zero) partial tile for the reduce
+  const bool no_k = kb0 >= kb1;
+  if (no_k && prm.splits == 1) return;
 
   // shared memory: [A stages][B stages] (1024-aligned) | barriers | tmem address
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -231,7 +257,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
         }
         umma_commit(&empty[s]);
       }
-      umma_commit(tmem_full);
+      if (kb0 < kb1) {
+        umma_commit(tmem_full);
+      } else {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(tmem_full)) : "memory");
+      }
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
@@ -243,35 +273,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
     __half* C = static_cast<__half*>(P.C);
     const __half* R = static_cast<const __half*>(P.R);
     const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
-    if (__all_sync(0xffffffffu, ok)) {
+    const bool all_ok = __all_sync(0xffffffffu, ok);
+    if (!P.ws) {
+      if (all_ok) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(trow + c0, v);  // all lanes execute (sync.aligned)
-        const int col = n0 + c0;
-        if (row < P.M && col < P.N) {
-          if (P.ws) {
-            float* W = P.ws + (size_t)row * P.N + col;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(trow + c0, v);  // all lanes execute (sync.aligned)
+          const int col = n0 + c0;
+          if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec);
+        }
+      }
+    } else {
+      // split-K: park this K-slice's fp32 tile; k_splitk_reduce sums the slices
+      if (all_ok) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(trow + c0, v);
+          if (no_k) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (col + i < P.N) atomicAdd(W + i, v[i]);
-          } else {
-            const size_t o = (size_t)row * P.ldc + col;
-            if (col + 16 <= P.N) {
-              uint4 pk[2];
-              __half2* h2 = reinterpret_cast<__half2*>(pk);
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+          }
+          const int col = n0 + c0;
+          if (row < P.M && col < P.N) {
+            float* dst = P.ws + ((size_t)split * P.M + row) * P.N + col;
+            if (col + 16 <= P.N && (P.N & 3) == 0) {
 #pragma unroll
-              for (int i = 0; i < 8; ++i) h2[i] = epi2<EPI>(v[2 * i], v[2 * i + 1], R, o + 2 * i);
-              if (vec) {
-                reinterpret_cast<uint4*>(C + o)[0] = pk[0];
-                reinterpret_cast<uint4*>(C + o)[1] = pk[1];
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) reinterpret_cast<__half2*>(C + o)[i] = h2[i];
-              }
+              for (int i = 0; i < 4; ++i)
+                reinterpret_cast<float4*>(dst)[i] =
+                    make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             } else {
-              for (int i = 0; i + 1 < 16 && col + i < P.N; i += 2)
-                *reinterpret_cast<__half2*>(C + o + i) = epi2<EPI>(v[i], v[i + 1], R, o + i);
+              for (int i = 0; i < 16 && col + i < P.N; ++i) dst[i] = v[i];
             }
           }
         }
@@ -285,18 +318,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
   }
 }
 
-// Split-K fixup: C = epi(ws), then ws = 0 for the next use. grid = M, block = 256.
+struct ReduceParams {
+  TcProblem p[4];
+  int n_problems, splits;
+};
+
+// Split-K reduce: C = epi(sum_s ws[s]) for every problem. grid = (ceil(max M*N/4 / 256), n).
 template <int EPI>
-__global__ void k_tc_fixup(float* __restrict__ ws, __half* __restrict__ C,
-                           const __half* __restrict__ R, int N, int ldc) {
-  const int m = blockIdx.x;
-  for (int c = threadIdx.x * 2; c < N; c += blockDim.x * 2) {
-    float* w = ws + (size_t)m * N + c;
-    const float2 acc = *reinterpret_cast<float2*>(w);
-    *reinterpret_cast<float2*>(w) = make_float2(0.f, 0.f);
-    const size_t o = (size_t)m * ldc + c;
-    *reinterpret_cast<__half2*>(C + o) = epi2<EPI>(acc.x, acc.y, R, o);
+__global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ ReduceParams rp) {
+  const TcProblem& P = rp.p[blockIdx.y];
+  const size_t MN = (size_t)P.M * P.N;
+  const size_t i = ((size_t)blockIdx.x * 256 + threadIdx.x) * 4;
+  if (i >= MN) return;
+  const int row = (int)(i / P.N), col = (int)(i % P.N);  // N % 4 == 0: 4 columns, one row
+  float4 acc = __ldcg(reinterpret_cast<const float4*>(P.ws + i));
+  for (int s = 1; s < rp.splits; ++s) {
+    const float4 q = __ldcg(reinterpret_cast<const float4*>(P.ws + s * MN + i));
+    acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
   }
+  __half* C = static_cast<__half*>(P.C);
+  const __half* R = static_cast<const __half*>(P.R);
+  const size_t o = (size_t)row * P.ldc + col;
+  const __half2 h0 = epi2<EPI>(acc.x, acc.y, R, o), h1 = epi2<EPI>(acc.z, acc.w, R, o + 2);
+  reinterpret_cast<__half2*>(C + o)[0] = h0;
+  reinterpret_cast<__half2*>(C + o)[1] = h1;
 }
 
 // ---------------------------------------------------------------------------
@@ -408,7 +453,8 @@ bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n) {
   return true;
 }
 
-// splits > 1 needs `ws` = zeroed fp32 scratch of sum_i M_i * N_i floats (re-zeroed on exit).
+// Split-K scratch: `ws` holds splits * sum_i M_i * N_i floats of partial tiles
+// (no initial value needed: every slice writes its whole tile).
 int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
                    cudaStream_t st) {
   TcParams prm;
@@ -417,7 +463,8 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, floa
   prm.splits = splits;
   constexpr int BN = 128;
   int gx = 0, gy = 0;
-  size_t ws_off = 0;
+  size_t ws_off = 0, total = 0;
+  for (int i = 0; i < n; ++i) total += (size_t)p[i].M * p[i].N;
   for (int i = 0; i < n; ++i) {
     int rc = make_map(&prm.ta[i], p[i].A, p[i].M, p[i].K, p[i].lda, BM);
     if (rc) return rc;
@@ -429,11 +476,12 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, floa
     prm.p[i].N = p[i].N;
     prm.p[i].K = p[i].K;
     prm.p[i].ldc = p[i].ldc;
-    prm.p[i].ws = splits > 1 ? ws + ws_off : nullptr;
+    prm.p[i].ws = splits > 1 ? ws + ws_off * splits : nullptr;
     ws_off += (size_t)p[i].M * p[i].N;
     gx = max(gx, (p[i].N + BN - 1) / BN);
     gy = max(gy, (p[i].M + BM - 1) / BM);
   }
+  (void)total;
   dim3 grid(gx, gy, n * splits);
   int rc;
   switch (epi) {
@@ -442,23 +490,21 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, floa
     default: rc = launch_tc<BN, RWKV_EPI_RELUSQ>(prm, grid, st); break;
   }
   if (rc || splits == 1) return rc;
+  ReduceParams rp;
+  rp.n_problems = n;
+  rp.splits = splits;
+  size_t max_mn = 0;
   for (int i = 0; i < n; ++i) {
-    __half* C = static_cast<__half*>(p[i].C);
-    const __half* R = static_cast<const __half*>(p[i].R);
-    switch (epi) {
-      case RWKV_EPI_STORE:
-        k_tc_fixup<RWKV_EPI_STORE><<<p[i].M, 256, 0, st>>>(prm.p[i].ws, C, R, p[i].N, p[i].ldc);
-        break;
-      case RWKV_EPI_RESID:
-        k_tc_fixup<RWKV_EPI_RESID><<<p[i].M, 256, 0, st>>>(prm.p[i].ws, C, R, p[i].N, p[i].ldc);
-        break;
-      default:
-        k_tc_fixup<RWKV_EPI_RELUSQ><<<p[i].M, 256, 0, st>>>(prm.p[i].ws, C, R, p[i].N, p[i].ldc);
-        break;
-    }
-    if ((rc = rwkv_check_launch("gemm_tc_fixup"))) return rc;
+    rp.p[i] = prm.p[i];
+    max_mn = max(max_mn, (size_t)p[i].M * p[i].N);
   }
-  return RWKV_OK;
+  dim3 rgrid((unsigned)((max_mn / 4 + 255) / 256), n);
+  switch (epi) {
+    case RWKV_EPI_STORE: k_splitk_reduce<RWKV_EPI_STORE><<<rgrid, 256, 0, st>>>(rp); break;
+    case RWKV_EPI_RESID: k_splitk_reduce<RWKV_EPI_RESID><<<rgrid, 256, 0, st>>>(rp); break;
+    default: k_splitk_reduce<RWKV_EPI_RELUSQ><<<rgrid, 256, 0, st>>>(rp); break;
+  }
+  return rwkv_check_launch("splitk_reduce");
 }
 
 // Host read of the device timeout flag (cleared on read); nonzero means a bounded wait gave up.
