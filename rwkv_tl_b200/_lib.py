@@ -27,6 +27,8 @@ EXPORTED = (
     "rwkv7_gemm_f16",
     "rwkv7_forward_workspace_bytes",
     "rwkv7_forward",
+    "rwkv7_decode_gemv_workspace_bytes",
+    "rwkv7_decode_gemv",
 )
 
 RWKV_OK, RWKV_ERR_ARG, RWKV_ERR_CUDA, RWKV_ERR_SPACE = 0, 1, 2, 3
@@ -117,6 +119,11 @@ def load() -> C.CDLL:
     lib.rwkv7_forward.restype = C.c_int
     lib.rwkv7_forward.argtypes = [C.POINTER(Model), C.POINTER(Batch), C.POINTER(StateDesc), vp,
                                   C.c_size_t, vp]
+    lib.rwkv7_decode_gemv_workspace_bytes.restype = C.c_size_t
+    lib.rwkv7_decode_gemv_workspace_bytes.argtypes = [C.POINTER(Model), C.c_int]
+    lib.rwkv7_decode_gemv.restype = C.c_int
+    lib.rwkv7_decode_gemv.argtypes = [C.POINTER(Model), vp, C.c_int, vp, C.POINTER(StateDesc),
+                                      vp, vp, C.c_size_t, vp]
     if lib.rwkv_b200_abi_version() != 1:
         raise RWKVError("librwkv_b200.so ABI version mismatch")
     _lib = lib

@@ -162,6 +162,8 @@ int check_model(const rwkv7_model* m) {
 
 }  // namespace
 
+int check_model_public(const rwkv7_model* m) { return check_model(m); }
+
 extern "C" size_t rwkv7_forward_workspace_bytes(const rwkv7_model* model, int n_rows, int n_seqs,
                                                 int n_logits) {
   if (check_model(model) || n_rows < 0 || n_seqs < 0 || n_logits < 0) return 0;

@@ -11,6 +11,7 @@ over many sequences (``decode_batch``, ``prefill_batch``, ``forward_batch``) on 
 
 from __future__ import annotations
 
+import os
 from abc import ABC, abstractmethod
 
 import torch
@@ -94,6 +95,7 @@ class RWKV7B200(RWKV7Model):
         self._cm = w.cmodel()
         self.max_rows = max_rows
         self._ws: Tensor | None = None
+        self._ws_dec: Tensor | None = None
         self._meta: dict = {}
         self.V = w.V
 
@@ -107,6 +109,27 @@ class RWKV7B200(RWKV7Model):
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.w.device)
         return self._ws.data_ptr(), self._ws.numel()
+
+    def _use_gemv(self, B: int) -> bool:
+        """Small batches take the fused GEMV decode path (RWKV_B200_DECODE=token forces
+        the token-batch path, =gemv the GEMV path)."""
+        mode = os.environ.get("RWKV_B200_DECODE", "")
+        if mode == "token":
+            return False
+        return B <= 8 and self.C % 256 == 0
+
+    def run_decode_gemv(self, tokens: Tensor, slots: Tensor | None, sdesc, logits: Tensor) -> None:
+        """One ``rwkv7_decode_gemv`` call (B <= 8 sequences, one token each)."""
+        B = tokens.numel()
+        need = self._lib.rwkv7_decode_gemv_workspace_bytes(self._cm, B)
+        if need == 0:
+            raise _lib.RWKVError("invalid model/batch for the decode GEMV path")
+        if self._ws_dec is None or self._ws_dec.numel() < need:
+            self._ws_dec = torch.empty(need, dtype=torch.uint8, device=self.w.device)
+        stream = torch.cuda.current_stream(self.w.device).cuda_stream
+        check(self._lib.rwkv7_decode_gemv(self._cm, ptr(tokens), B, ptr(slots), sdesc,
+                                          ptr(logits), self._ws_dec.data_ptr(),
+                                          self._ws_dec.numel(), stream))
 
     def _arange(self, n: int) -> Tensor:
         key = ("arange", n)
@@ -180,8 +203,11 @@ class RWKV7B200(RWKV7Model):
             raise ValueError(f"decode expects one token, got {tok.numel()}")
         d, slot, back = self._state_desc(S)
         logits = torch.empty(1, self.V, dtype=torch.float16, device=self.w.device)
-        self.run_batch(tok, self._const((0, 1)), self._zeros(1), slot, d, self._zeros(1), logits,
-                       SEM_DECODE)
+        if self._use_gemv(1):
+            self.run_decode_gemv(tok, slot, d, logits)
+        else:
+            self.run_batch(tok, self._const((0, 1)), self._zeros(1), slot, d, self._zeros(1),
+                           logits, SEM_DECODE)
         if back:
             back()
         return logits[0], S
@@ -219,6 +245,9 @@ class RWKV7B200(RWKV7Model):
             raise ValueError(f"{B} tokens but only {state.n_slots} state slots")
         if logits is None:
             logits = torch.empty(B, self.V, dtype=torch.float16, device=self.w.device)
+        if self._use_gemv(B):
+            self.run_decode_gemv(tok, slots, state.desc(), logits)
+            return logits
         rows = self._arange(B + 1)
         for s in range(0, B, self.max_rows):
             n = min(self.max_rows, B - s)
