@@ -183,7 +183,7 @@ int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* batch,
  * chained with programmatic dependent launch so each kernel's weights stream
  * into L2 while the previous kernel finishes. Decode rounding semantics.
  * tokens: device int64 [n_seqs]; slots: device int [n_seqs] or NULL; logits:
- * fp16 [n_seqs, V]. n_embd must be a multiple of 256. Same result as
+ * fp16 [n_seqs, V]. n_embd must be 768 or 1024. Same result as
  * rwkv7_forward with RWKV_SEM_DECODE on one token per sequence. */
 size_t rwkv7_decode_gemv_workspace_bytes(const rwkv7_model* model, int n_seqs);
 int rwkv7_decode_gemv(const rwkv7_model* model, const int64_t* tokens, int n_seqs,

@@ -116,7 +116,7 @@ class RWKV7B200(RWKV7Model):
         mode = os.environ.get("RWKV_B200_DECODE", "")
         if mode == "token":
             return False
-        return B <= 8 and self.C % 256 == 0
+        return B <= 4 and self.C in (768, 1024)
 
     def run_decode_gemv(self, tokens: Tensor, slots: Tensor | None, sdesc, logits: Tensor) -> None:
         """One ``rwkv7_decode_gemv`` call (B <= 8 sequences, one token each)."""
