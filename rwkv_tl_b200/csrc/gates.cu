@@ -33,19 +33,31 @@ __global__ void __launch_bounds__(256) k_gates(
   const int h = blockIdx.y, m_base = blockIdx.x * GT_ROWS;
   const int hc = h * RWKV_HD;
 
-  // stage weights: 288 rows x 128 bytes (8 x 16B chunks per row)
+  // stage weights asynchronously: 288 rows x 128 bytes (8 x 16B chunks per row)
   for (int i = tid; i < RWKV_RANK_SUM * 8; i += 256) {
     const int j = i >> 3, q = i & 7;
-    *reinterpret_cast<uint4*>(sw + j * 64 + q * 8) =
-        *reinterpret_cast<const uint4*>(w_up + (size_t)j * C + hc + q * 8);
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(sw + j * 64 + q * 8));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d),
+                 "l"(w_up + (size_t)j * C + hc + q * 8));
   }
-  // stage activated ranks
-  for (int i = tid; i < GT_ROWS * RWKV_RANK_SUM; i += 256) {
+  asm volatile("cp.async.commit_group;\n" ::);
+  // stage activated ranks (all 18 loads per thread issued before use)
+  constexpr int PER = GT_ROWS * RWKV_RANK_SUM / 256;
+  __half rv[PER];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int i = tid + 256 * u;
+    const int m = m_base + i / RWKV_RANK_SUM;
+    rv[u] = m < M ? ranks[(size_t)m * RWKV_RANK_SUM + i % RWKV_RANK_SUM] : __float2half(0.f);
+  }
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int i = tid + 256 * u;
     const int r = i / RWKV_RANK_SUM, j = i % RWKV_RANK_SUM;
     const int m = m_base + r;
     float val = 0.f;
     if (m < M) {
-      val = h2f(ranks[(size_t)m * RWKV_RANK_SUM + j]);
+      val = h2f(rv[u]);
       if (j >= 32 && j < 96) {
         val = tanhf(val);
         if (SEM == SEM_PREFILL) val = r16(val);
@@ -56,6 +68,7 @@ __global__ void __launch_bounds__(256) k_gates(
     }
     sr[i] = val;
   }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   __syncthreads();
 
   const int r0 = 2 * warp;

@@ -227,7 +227,7 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, floa
 
 // Kernel choice by shape: the tcgen05 kernel when every problem has K % 64 == 0
 // (all model projections), else the mma.sync kernel. Small output grids are
-// split along K to fill the 148 SMs (at least 4 K-blocks per slice): `ws`
+// split along K to fill the 148 SMs (at least 8 K-blocks per slice): `ws`
 // (ws_floats floats) takes the fp32 partial tiles, reduced by a second kernel.
 // RWKV_B200_GEMM=mma|tc forces a kernel.
 int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
@@ -248,8 +248,10 @@ int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws
   int splits = 1;
   bool n4 = true;
   for (int i = 0; i < n; ++i) n4 = n4 && (problems[i].N % 4 == 0) && (problems[i].ldc % 2 == 0);
-  if (ws && n4 && tiles < 148) {
-    splits = max(1, min(min_kb / 4, (2 * 148 + tiles - 1) / tiles));
+  if (ws && n4 && tiles < 48) {
+    // enough CTAs to cover the SMs, but at least 8 K-blocks (512) per slice: split-K
+    // moves splits * M * N * 8 bytes of partials, which must stay small beside the weights
+    splits = max(1, min(min_kb / 8, (128 + tiles - 1) / tiles));
     while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
   }
   (void)gx;

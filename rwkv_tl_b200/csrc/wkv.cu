@@ -42,20 +42,50 @@ __device__ __forceinline__ void load_tok(TokVec& t, const __half* r, const __hal
   }
 }
 
-// One recurrence step on the warp's 8 rows; returns y for row 8*warp+j in y[j]
-// (every lane holds all 8 sums).
+// Sum 8 per-lane partials across the warp with 9 shuffles (halving exchange);
+// lane l ends with the total of index (l >> 2) & 7.
+__device__ __forceinline__ float reduce8(float (&p)[8], int lane) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool up = lane & 16;
+    const float send = up ? p[i] : p[i + 4];
+    const float keep = up ? p[i + 4] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool up = lane & 8;
+    const float send = up ? p[i] : p[i + 2];
+    const float keep = up ? p[i + 2] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const bool up = lane & 4;
+    const float send = up ? p[0] : p[1];
+    const float keep = up ? p[1] : p[0];
+    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  p[0] += __shfl_xor_sync(0xffffffffu, p[0], 2);
+  return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
+}
+
+// One recurrence step on the warp's 8 rows; y[j] (row 8*warp+j) is valid in lane 4j.
 __device__ __forceinline__ void wkv_step(float2 (&s)[8], const TokVec& t, float (&y)[8]) {
+  const int lane = threadIdx.x & 31;
+  float p[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) p[j] = s[j].x * t.a.x + s[j].y * t.a.y;
+  const float sa_mine = reduce8(p, lane);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    float sa = s[j].x * t.a.x;
-    sa += s[j].y * t.a.y;
-    sa = warp_sum(sa);
+    const float sa = __shfl_sync(0xffffffffu, sa_mine, 4 * j);
     s[j].x = s[j].x * t.w.x + sa * t.b.x + t.v[j] * t.k.x;
     s[j].y = s[j].y * t.w.y + sa * t.b.y + t.v[j] * t.k.y;
-    float p = s[j].x * t.r.x;
-    p += s[j].y * t.r.y;
-    y[j] = warp_sum(p);
+    p[j] = s[j].x * t.r.x + s[j].y * t.r.y;
   }
+  const float y_mine = reduce8(p, lane);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) y[j] = __shfl_sync(0xffffffffu, y_mine, 4 * j);
 }
 
 __device__ __forceinline__ void load_state(float2 (&s)[8], const float* S, int lane, int warp) {
@@ -215,11 +245,75 @@ template __global__ void k_wkv_tokens<SEM_PREFILL>(const __half*, const __half*,
                                                    const __half*, const __half*, float*, const int*,
                                                    const int*, __half*, int);
 
+// One token per sequence (batched decode): grid = (n_seqs, H), 256 threads. All
+// state loads of a warp are issued together and no next-token buffer is kept, so the
+// kernel stays small enough for 5 CTAs per SM (enough bytes in flight to stream the
+// 2 x 16 KiB of state per (sequence, head) at HBM rate).
+template <int SEM>
+__global__ void __launch_bounds__(256, 5) k_wkv_decode(
+    const __half* __restrict__ rbuf, const __half* __restrict__ gbuf, size_t plane,
+    const __half* __restrict__ r_k, const __half* __restrict__ lnx_w,
+    const __half* __restrict__ lnx_b, float* __restrict__ rnn, const int* __restrict__ slots,
+    __half* __restrict__ yg, int C) {
+  __shared__ float ybuf[RWKV_HD];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = blockIdx.x, h = blockIdx.y, H = gridDim.y;
+  const int slot = slots ? slots[m] : m;
+  float* Sh = rnn + ((size_t)slot * H + h) * RWKV_HD * RWKV_HD;
+  float2 s[8];
+  load_state(s, Sh, lane, warp);
+  const int hc = h * RWKV_HD;
+  const size_t o = (size_t)m * C + hc;
+  TokVec t;
+  load_tok(t, rbuf + o, gbuf + o, gbuf + plane + o, gbuf + 2 * plane + o, gbuf + 3 * plane + o,
+           gbuf + 4 * plane + o, lane, warp);
+  float yy[8];
+  wkv_step(s, t, yy);
+  store_state(s, Sh, lane, warp);
+  if ((lane & 3) == 0) ybuf[8 * warp + (lane >> 2)] = r16(yy[lane >> 2]);
+  __syncthreads();
+  if (warp == 0) {
+    const size_t oc = o + 2 * lane;
+    const float2 y = make_float2(ybuf[2 * lane], ybuf[2 * lane + 1]);
+    const float mean = warp_sum(y.x + y.y) * (1.0f / RWKV_HD);
+    const float dx = y.x - mean, dy = y.y - mean;
+    const float var = warp_sum(dx * dx + dy * dy) * (1.0f / RWKV_HD);
+    const float rstd = 1.0f / sqrtf(var + 64e-5f);
+    const float2 rk = ld_h2(r_k + hc + 2 * lane), lw = ld_h2(lnx_w + hc + 2 * lane),
+                 lb = ld_h2(lnx_b + hc + 2 * lane);
+    const float2 rr = ld_h2(rbuf + oc), kk = ld_h2(gbuf + plane + oc),
+                 vv = ld_h2(gbuf + 2 * plane + oc), gg = ld_h2(gbuf + 5 * plane + oc);
+    float ox, oy;
+    if (SEM == SEM_DECODE) {
+      float p = rr.x * kk.x * rk.x;
+      p += rr.y * kk.y * rk.y;
+      const float rkrk = warp_sum(p);
+      ox = r16(dx * rstd * lw.x + lb.x + rkrk * vv.x);
+      oy = r16(dy * rstd * lw.y + lb.y + rkrk * vv.y);
+    } else {
+      const float fx = r16(dx * rstd * lw.x + lb.x), fy = r16(dy * rstd * lw.y + lb.y);
+      const float rkrk = r16(warp_sum(r16(r16(rr.x * kk.x) * rk.x) + r16(r16(rr.y * kk.y) * rk.y)));
+      ox = r16(fx + r16(rkrk * vv.x));
+      oy = r16(fy + r16(rkrk * vv.y));
+    }
+    *reinterpret_cast<__half2*>(yg + oc) = __floats2half2_rn(ox * gg.x, oy * gg.y);
+  }
+}
+
 int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t plane,
                       const __half* r_k, const __half* lnx_w, const __half* lnx_b, float* rnn,
                       const int* cu, const int* slots, __half* yg, int n_seqs, int H, int C,
                       cudaStream_t st) {
   dim3 grid(n_seqs, H);
+  if (n_seqs * C == (int)plane) {  // one token per sequence
+    if (sem == SEM_DECODE)
+      k_wkv_decode<SEM_DECODE><<<grid, 256, 0, st>>>(rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn,
+                                                     slots, yg, C);
+    else
+      k_wkv_decode<SEM_PREFILL><<<grid, 256, 0, st>>>(rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn,
+                                                      slots, yg, C);
+    return rwkv_check_launch("wkv_decode");
+  }
   if (sem == SEM_DECODE)
     k_wkv_tokens<SEM_DECODE><<<grid, 256, 0, st>>>(rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn, cu,
                                                    slots, yg, C);

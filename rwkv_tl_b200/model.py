@@ -116,6 +116,8 @@ class RWKV7B200(RWKV7Model):
         mode = os.environ.get("RWKV_B200_DECODE", "")
         if mode == "token":
             return False
+        if mode == "gemv":
+            return B <= 8 and self.C in (768, 1024)
         return B <= 4 and self.C in (768, 1024)
 
     def run_decode_gemv(self, tokens: Tensor, slots: Tensor | None, sdesc, logits: Tensor) -> None:
