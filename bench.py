@@ -17,7 +17,9 @@ Inputs (weights 0.77 GB + states 3.3 GB per GPU) are far larger than the
   copies the B token ids from pinned host memory, runs ``decode_batch`` (CUDA
   graph), takes the greedy argmax on the device and reads the B next-token ids
   back into pinned host memory (synchronised).
-* ``roofline``: the dominant kernel of the step timed alone on the same stream.
+* ``roofline``: the dominant kernel of the step (the one-token wkv7 + GroupNorm +
+  gate kernel, 22% of the step in the ncu launch list) timed alone with CUDA events
+  on the launching stream; ``step_roofline``: the whole step against HBM.
 * ``cpu_baseline``: the CPU oracle port of the reference's pure-torch model
   (``oracle/``) decoding a bounded sample on the host cores (rank 0, N=1).
 * ``--impl reference``: only the CPU port, on all host threads (rank 0).
@@ -65,7 +67,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -256,14 +258,13 @@ def run_b200(args, world, rank, local):
     e2e_ms = max_over_ranks(e2e_ms, world)
     e2e_val = world * B / (e2e_ms * 1e-3)
 
-    # ---- roofline of the step (HBM bound): algorithmic bytes per step ----
+    # ---- roofline: the whole step, and its dominant kernel timed alone ----
     pk, pk_kind = peaks()
     wbytes = w.nbytes() - 2 * w.emb.numel()  # weights streamed per step (emb: rows only)
     state_bytes = B * w.L * (w.H * 64 * 64 * 4 * 2 + 2 * w.C * 2 * 2)
     io_bytes = B * (w.C * 2 + cfg.vocab * 2)
     step_bytes = wbytes + state_bytes + io_bytes
-    achieved = step_bytes / (ms * 1e-3) / 1e9
-
+    kern = wkv_kernel_roofline(lib, B, w.H, dev, stream, pk["hbm_gbs"])
     extra = {}
     if rank == 0 and world == 1 and not args.quick:
         extra = side_measurements(model, w, dev, stream)
@@ -283,16 +284,63 @@ def run_b200(args, world, rank, local):
             "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": B * 8,
                     "d2h_bytes_per_step": B * 8},
             "gpu_launches": launches_per_step * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "whole decode step (all kernels, one graph)",
-                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind,
-                         "traffic": None, "algorithmic_bytes_per_step": step_bytes},
+            "roofline": dict(kern, peak_kind=pk_kind),
+            "step_roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes,
+                              "achieved": step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+                              "frac": step_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]},
             "clocks": clocks,
         }
         line.update(extra)
         if world == 1 and not args.quick:
             line["cpu_baseline"] = cpu_decode_rate(args.cpu_tokens, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)
+
+
+def profile_traffic(name: str) -> float | None:
+    """DRAM bytes per launch recorded from an ncu capture (profiles/<name>.txt)."""
+    p = REPO / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+def wkv_kernel_roofline(lib, B: int, H: int, dev, stream, peak: float) -> dict:
+    """Dominant kernel of the batched decode step: the one-token wkv7 + GroupNorm + gate
+    kernel (rwkv7_wkv_gn_step), timed alone with CUDA events on the launching stream
+    over the same shapes as one layer of the step (B sequences, H heads)."""
+    from rwkv_tl_b200 import _lib
+
+    C = H * 64
+    g = torch.Generator(device=dev).manual_seed(7)
+    # one state block per layer, as in the step: 24 x 67 MB, far beyond the 126 MB L2
+    states = [0.1 * torch.randn(B, H, 64, 64, generator=g, device=dev) for _ in range(24)]
+    vec = [torch.randn(B, C, generator=g, device=dev).half() for _ in range(7)]
+    cst = [torch.randn(C, generator=g, device=dev).half() for _ in range(3)]
+    out = torch.empty(B, C, dtype=torch.float16, device=dev)
+    h = stream.cuda_stream
+
+    it = [0]
+
+    def launch():
+        S = states[it[0] % len(states)]
+        it[0] += 1
+        _lib.check(lib.rwkv7_wkv_gn_step(S.data_ptr(), None, *[t.data_ptr() for t in vec],
+                                         *[t.data_ptr() for t in cst], out.data_ptr(), B, H, 0, h))
+
+    for _ in range(5):
+        launch()
+    n = 240  # ten passes over the 24 state blocks
+    ms = timed(launch, n, stream)
+    # per launch: fp32 state read + write, 7 fp16 input vectors, 1 fp16 output vector
+    algo = B * H * 64 * 64 * 4 * 2 + 8 * B * C * 2
+    achieved = algo / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": "k_wkv_decode (rwkv7_wkv_gn_step), one layer of the step",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": profile_traffic("wkv_decode_b256"), "algorithmic_bytes_per_launch": algo,
+            "avg_launch_us": ms * 1e3}
 
 
 def side_measurements(model, w, dev, stream) -> dict:
@@ -345,8 +393,8 @@ def run_profile(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--cpu-tokens", type=int, default=4)

@@ -129,6 +129,19 @@ int rwkv_b200_device_error(void);
 int rwkv7_dplr_step(void* S, const void* r, const void* w, const void* k, const void* v,
                     const void* a, const void* b, void* y, int n_seq, int H, void* stream);
 
+/* One decode token of n_seq sequences through the whole per-head attention tail:
+ * the wkv7 step above on state S[slots[i]] (slots NULL: i), then per-head GroupNorm
+ * (eps 64e-5, affine lnx_w/lnx_b), the bonus (sum_j r*k*r_k) * v and the g gate:
+ *   out = (GN(y) + bonus) * g      (fp16 rounding points of `semantics`)
+ * r, w, k, v, a, b, g, out: fp16 [n_seq, H*64]; r_k, lnx_w, lnx_b: fp16 [H*64];
+ * S: fp32 [slots, H, 64, 64]. Replaces fused_dplr + fused_gn_rkrk and the g
+ * multiply of the decode TMIX (src/rwkv_tl/kernels/dplr.py:237-270,
+ * demo/_rwkv7_base.py:202-206). */
+int rwkv7_wkv_gn_step(void* S, const int* slots, const void* r, const void* w, const void* k,
+                      const void* v, const void* a, const void* b, const void* g,
+                      const void* r_k, const void* lnx_w, const void* lnx_b, void* out,
+                      int n_seq, int H, int semantics, void* stream);
+
 /* The same recurrence over T consecutive tokens of one sequence (fused_dplr_T):
  * r..b, y: fp16 [T, H, 64]; S: fp32 [H, 64, 64] updated in place. */
 int rwkv7_dplr_seq(void* S, const void* r, const void* w, const void* k, const void* v,

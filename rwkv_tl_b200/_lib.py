@@ -21,6 +21,7 @@ EXPORTED = (
     "rwkv_b200_device_error",
     "rwkv7_dplr_step",
     "rwkv7_dplr_seq",
+    "rwkv7_wkv_gn_step",
     "rwkv7_dplr_chunked_workspace_bytes",
     "rwkv7_dplr_chunked",
     "rwkv7_dplr_chunked_noalloc",
@@ -112,6 +113,8 @@ def load() -> C.CDLL:
     lib.rwkv7_dplr_chunked.argtypes = [vp] * 8 + [C.c_int] * 3 + [vp, C.c_size_t, vp]
     lib.rwkv7_dplr_chunked_noalloc.restype = C.c_int
     lib.rwkv7_dplr_chunked_noalloc.argtypes = [vp] * 8 + [C.c_int] * 3 + [vp]
+    lib.rwkv7_wkv_gn_step.restype = C.c_int
+    lib.rwkv7_wkv_gn_step.argtypes = [vp] * 13 + [C.c_int, C.c_int, C.c_int, vp]
     lib.rwkv7_gemm_f16.restype = C.c_int
     lib.rwkv7_gemm_f16.argtypes = [C.POINTER(GemmProblem), C.c_int, C.c_int, vp]
     lib.rwkv7_forward_workspace_bytes.restype = C.c_size_t

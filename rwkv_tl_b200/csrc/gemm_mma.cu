@@ -222,41 +222,18 @@ int gemm_mma_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStre
 }
 
 bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n);
-int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
+int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_t ws_floats,
                    cudaStream_t st);
 
 // Kernel choice by shape: the tcgen05 kernel when every problem has K % 64 == 0
-// (all model projections), else the mma.sync kernel. Small output grids are
-// split along K to fill the 148 SMs (at least 8 K-blocks per slice): `ws`
-// (ws_floats floats) takes the fp32 partial tiles, reduced by a second kernel.
-// RWKV_B200_GEMM=mma|tc forces a kernel.
+// (all model projections; it picks its tile shape and split-K itself, `ws` being
+// the split-K scratch), else the mma.sync kernel. RWKV_B200_GEMM=mma|tc forces one.
 int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
                    size_t ws_floats, cudaStream_t st) {
   const char* e = getenv("RWKV_B200_GEMM");
   const bool force_mma = e && e[0] == 'm';
   if (force_mma || !gemm_tc_eligible(problems, n)) return gemm_mma_launch(problems, n, epi, st);
-  int tiles = 0, min_kb = 1 << 30, gx = 0, gy = 0;
-  size_t mn = 0;
-  for (int i = 0; i < n; ++i) {
-    const int tx = (problems[i].N + 127) / 128, ty = (problems[i].M + 127) / 128;
-    tiles += tx * ty;
-    gx = max(gx, tx);
-    gy = max(gy, ty);
-    min_kb = min(min_kb, problems[i].K / 64);
-    mn += (size_t)problems[i].M * problems[i].N;
-  }
-  int splits = 1;
-  bool n4 = true;
-  for (int i = 0; i < n; ++i) n4 = n4 && (problems[i].N % 4 == 0) && (problems[i].ldc % 2 == 0);
-  if (ws && n4 && tiles < 48) {
-    // enough CTAs to cover the SMs, but at least 8 K-blocks (512) per slice: split-K
-    // moves splits * M * N * 8 bytes of partials, which must stay small beside the weights
-    splits = max(1, min(min_kb / 8, (128 + tiles - 1) / tiles));
-    while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
-  }
-  (void)gx;
-  (void)gy;
-  return gemm_tc_launch(problems, n, epi, splits, ws, st);
+  return gemm_tc_launch(problems, n, epi, ws, ws_floats, st);
 }
 
 int gemm_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStream_t st) {

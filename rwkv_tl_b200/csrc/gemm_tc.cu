@@ -29,7 +29,7 @@
 
 namespace {
 
-constexpr int BM = 128, BK = 64, STAGES = 3;  // 3 stages: two CTAs share an SM
+constexpr int BM = 128, BK = 64;
 constexpr int NTHREADS = 192;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 
@@ -175,8 +175,8 @@ __device__ __forceinline__ void store16(const float (&v)[16], __half* C, const _
   }
 }
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(NTHREADS, 2) k_gemm_tc(const __grid_constant__ TcParams prm) {
+template <int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__ TcParams prm) {
   extern __shared__ unsigned char smem_raw[];
   const int g = blockIdx.z % prm.n_problems;
   const int split = blockIdx.z / prm.n_problems;
@@ -416,27 +416,27 @@ int make_map(CUtensorMap* out, const void* ptr, int rows, int cols, int ld, int 
   return RWKV_OK;
 }
 
-template <int BN>
+template <int BN, int STAGES>
 constexpr int smem_bytes() {
   return 1024 + STAGES * (BM * BK * 2 + BN * BK * 2) + (2 * STAGES + 1) * 8 + 16;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int STAGES>
 int launch_tc(const TcParams& prm, dim3 grid, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   static bool done[64] = {};
   if (dev < 64 && !done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN, EPI>,
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN, EPI, STAGES>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smem_bytes<BN>());
+                                         smem_bytes<BN, STAGES>());
     if (e != cudaSuccess) {
       rwkv_set_error("gemm_tc: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return RWKV_ERR_CUDA;
     }
     done[dev] = true;
   }
-  k_gemm_tc<BN, EPI><<<grid, NTHREADS, smem_bytes<BN>(), st>>>(prm);
+  k_gemm_tc<BN, EPI, STAGES><<<grid, NTHREADS, smem_bytes<BN, STAGES>(), st>>>(prm);
   return rwkv_check_launch("gemm_tc");
 }
 
@@ -453,15 +453,43 @@ bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n) {
   return true;
 }
 
-// Split-K scratch: `ws` holds splits * sum_i M_i * N_i floats of partial tiles
-// (no initial value needed: every slice writes its whole tile).
-int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
+template <int BN, int STAGES>
+int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
+                       cudaStream_t st);
+
+// Tile configuration and split-K by problem size. Large grids: 128 x 128 tiles,
+// 3 stages (two CTAs per SM). Small grids (batched decode): 128 x 64 tiles with 6
+// stages (144 KiB of operands in flight per CTA) and, when still fewer than 48
+// tiles, a K split with at least 8 K-blocks per slice. `ws` takes the split-K fp32
+// partial tiles (ws_floats floats; no initial value needed).
+int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_t ws_floats,
                    cudaStream_t st) {
+  int tiles128 = 0, tiles64 = 0, min_kb = 1 << 30;
+  size_t mn = 0;
+  bool n4 = true;
+  for (int i = 0; i < n; ++i) {
+    tiles128 += ((p[i].M + BM - 1) / BM) * ((p[i].N + 127) / 128);
+    tiles64 += ((p[i].M + BM - 1) / BM) * ((p[i].N + 63) / 64);
+    min_kb = min(min_kb, p[i].K / BK);
+    mn += (size_t)p[i].M * p[i].N;
+    n4 = n4 && p[i].N % 4 == 0 && p[i].ldc % 2 == 0;
+  }
+  if (tiles128 >= 148) return gemm_tc_launch_cfg<128, 3>(p, n, epi, 1, ws, st);
+  int splits = 1;
+  if (ws && n4 && tiles64 < 48) {
+    splits = max(1, min(min_kb / 8, (128 + tiles64 - 1) / tiles64));
+    while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
+  }
+  return gemm_tc_launch_cfg<64, 6>(p, n, epi, splits, ws, st);
+}
+
+template <int BN, int STAGES>
+int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
+                       cudaStream_t st) {
   TcParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.n_problems = n;
   prm.splits = splits;
-  constexpr int BN = 128;
   int gx = 0, gy = 0;
   size_t ws_off = 0, total = 0;
   for (int i = 0; i < n; ++i) total += (size_t)p[i].M * p[i].N;
@@ -485,9 +513,9 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, int splits, floa
   dim3 grid(gx, gy, n * splits);
   int rc;
   switch (epi) {
-    case RWKV_EPI_STORE: rc = launch_tc<BN, RWKV_EPI_STORE>(prm, grid, st); break;
-    case RWKV_EPI_RESID: rc = launch_tc<BN, RWKV_EPI_RESID>(prm, grid, st); break;
-    default: rc = launch_tc<BN, RWKV_EPI_RELUSQ>(prm, grid, st); break;
+    case RWKV_EPI_STORE: rc = launch_tc<BN, RWKV_EPI_STORE, STAGES>(prm, grid, st); break;
+    case RWKV_EPI_RESID: rc = launch_tc<BN, RWKV_EPI_RESID, STAGES>(prm, grid, st); break;
+    default: rc = launch_tc<BN, RWKV_EPI_RELUSQ, STAGES>(prm, grid, st); break;
   }
   if (rc || splits == 1) return rc;
   ReduceParams rp;

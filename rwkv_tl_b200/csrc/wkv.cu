@@ -249,10 +249,13 @@ template __global__ void k_wkv_tokens<SEM_PREFILL>(const __half*, const __half*,
 // state loads of a warp are issued together and no next-token buffer is kept, so the
 // kernel stays small enough for 5 CTAs per SM (enough bytes in flight to stream the
 // 2 x 16 KiB of state per (sequence, head) at HBM rate).
+struct DecVecs {
+  const __half *r, *w, *k, *v, *a, *b, *g;  // [n_seqs, C] each
+};
+
 template <int SEM>
 __global__ void __launch_bounds__(256, 5) k_wkv_decode(
-    const __half* __restrict__ rbuf, const __half* __restrict__ gbuf, size_t plane,
-    const __half* __restrict__ r_k, const __half* __restrict__ lnx_w,
+    const DecVecs X, const __half* __restrict__ r_k, const __half* __restrict__ lnx_w,
     const __half* __restrict__ lnx_b, float* __restrict__ rnn, const int* __restrict__ slots,
     __half* __restrict__ yg, int C) {
   __shared__ float ybuf[RWKV_HD];
@@ -265,8 +268,7 @@ __global__ void __launch_bounds__(256, 5) k_wkv_decode(
   const int hc = h * RWKV_HD;
   const size_t o = (size_t)m * C + hc;
   TokVec t;
-  load_tok(t, rbuf + o, gbuf + o, gbuf + plane + o, gbuf + 2 * plane + o, gbuf + 3 * plane + o,
-           gbuf + 4 * plane + o, lane, warp);
+  load_tok(t, X.r + o, X.w + o, X.k + o, X.v + o, X.a + o, X.b + o, lane, warp);
   float yy[8];
   wkv_step(s, t, yy);
   store_state(s, Sh, lane, warp);
@@ -281,8 +283,8 @@ __global__ void __launch_bounds__(256, 5) k_wkv_decode(
     const float rstd = 1.0f / sqrtf(var + 64e-5f);
     const float2 rk = ld_h2(r_k + hc + 2 * lane), lw = ld_h2(lnx_w + hc + 2 * lane),
                  lb = ld_h2(lnx_b + hc + 2 * lane);
-    const float2 rr = ld_h2(rbuf + oc), kk = ld_h2(gbuf + plane + oc),
-                 vv = ld_h2(gbuf + 2 * plane + oc), gg = ld_h2(gbuf + 5 * plane + oc);
+    const float2 rr = ld_h2(X.r + oc), kk = ld_h2(X.k + oc), vv = ld_h2(X.v + oc),
+                 gg = ld_h2(X.g + oc);
     float ox, oy;
     if (SEM == SEM_DECODE) {
       float p = rr.x * kk.x * rk.x;
@@ -306,12 +308,12 @@ int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t pl
                       cudaStream_t st) {
   dim3 grid(n_seqs, H);
   if (n_seqs * C == (int)plane) {  // one token per sequence
+    const DecVecs X = {rbuf, gbuf, gbuf + plane, gbuf + 2 * plane, gbuf + 3 * plane,
+                       gbuf + 4 * plane, gbuf + 5 * plane};
     if (sem == SEM_DECODE)
-      k_wkv_decode<SEM_DECODE><<<grid, 256, 0, st>>>(rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn,
-                                                     slots, yg, C);
+      k_wkv_decode<SEM_DECODE><<<grid, 256, 0, st>>>(X, r_k, lnx_w, lnx_b, rnn, slots, yg, C);
     else
-      k_wkv_decode<SEM_PREFILL><<<grid, 256, 0, st>>>(rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn,
-                                                      slots, yg, C);
+      k_wkv_decode<SEM_PREFILL><<<grid, 256, 0, st>>>(X, r_k, lnx_w, lnx_b, rnn, slots, yg, C);
     return rwkv_check_launch("wkv_decode");
   }
   if (sem == SEM_DECODE)
@@ -350,4 +352,30 @@ extern "C" int rwkv7_dplr_seq(void* S, const void* r, const void* w, const void*
                                                   (const __half*)a, (const __half*)b, (__half*)y,
                                                   T, H);
   return rwkv_check_launch("rwkv7_dplr_seq");
+}
+
+extern "C" int rwkv7_wkv_gn_step(void* S, const int* slots, const void* r, const void* w,
+                                 const void* k, const void* v, const void* a, const void* b,
+                                 const void* g, const void* r_k, const void* lnx_w,
+                                 const void* lnx_b, void* out, int n_seq, int H, int semantics,
+                                 void* stream) {
+  if (!S || !r || !w || !k || !v || !a || !b || !g || !r_k || !lnx_w || !lnx_b || !out ||
+      n_seq <= 0 || H <= 0 || (semantics != SEM_DECODE && semantics != SEM_PREFILL)) {
+    rwkv_set_error("rwkv7_wkv_gn_step: null pointer or bad size (n_seq=%d, H=%d)", n_seq, H);
+    return RWKV_ERR_ARG;
+  }
+  const int C = H * RWKV_HD;
+  const DecVecs X = {(const __half*)r, (const __half*)w, (const __half*)k, (const __half*)v,
+                     (const __half*)a, (const __half*)b, (const __half*)g};
+  dim3 grid(n_seq, H);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (semantics == SEM_DECODE)
+    k_wkv_decode<SEM_DECODE><<<grid, 256, 0, st>>>(X, (const __half*)r_k, (const __half*)lnx_w,
+                                                   (const __half*)lnx_b, (float*)S, slots,
+                                                   (__half*)out, C);
+  else
+    k_wkv_decode<SEM_PREFILL><<<grid, 256, 0, st>>>(X, (const __half*)r_k, (const __half*)lnx_w,
+                                                    (const __half*)lnx_b, (float*)S, slots,
+                                                    (__half*)out, C);
+  return rwkv_check_launch("rwkv7_wkv_gn_step");
 }

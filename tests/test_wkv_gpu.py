@@ -120,3 +120,47 @@ def test_dplr_chunked_config1(B, T):
     torch.cuda.synchronize()
     assert rel_l2(S, Sref) < 1e-4
     assert rel_l2(y.float(), yref) < 1e-3
+
+
+@pytest.mark.parametrize("B", [1, 37, 256])
+def test_wkv_gn_step_decode(B):
+    """wkv7 step + GroupNorm + bonus + g gate (fused_dplr + fused_gn_rkrk + (y*g)),
+    decode rounding points, against an fp64 torch restatement."""
+    from rwkv_tl_b200 import _lib
+
+    lib = _lib.load()
+    H, C = 16, 1024
+    r, w, k, v, A, Bv, S0 = _inputs(B, 1, H, seed=500 + B)
+    g = torch.Generator().manual_seed(B)
+    gate = torch.randn(B, C, generator=g).half()
+    r_k = (0.1 * torch.randn(C, generator=g)).half()
+    lnw = (1 + 0.1 * torch.randn(C, generator=g)).half()
+    lnb = (0.1 * torch.randn(C, generator=g)).half()
+    slots = torch.randperm(B, generator=g).to(torch.int32)
+    S_slot = torch.empty_like(S0)
+    S_slot[slots.long()] = S0  # sequence i lives in slot slots[i]
+    vecs = [t[:, 0].reshape(B, C) for t in (r, w, k, v, A, Bv)]
+    # reference (fp64, fp16 stores where the decode kernels store)
+    d = lambda t: t.double()  # noqa: E731
+    S = d(S0)
+    rr, ww, kk, vv, aa, bb = (d(t).reshape(B, H, 64) for t in vecs)
+    sa = torch.einsum("bhvk,bhk->bhv", S, aa)
+    S = S * ww[:, :, None, :] + sa[..., None] * bb[:, :, None, :] + vv[..., None] * kk[:, :, None, :]
+    y = torch.einsum("bhvk,bhk->bhv", S, rr).half().double()
+    mean = y.mean(-1, keepdim=True)
+    var = ((y - mean) ** 2).mean(-1, keepdim=True)
+    yn = ((y - mean) / torch.sqrt(var + 64e-5)).reshape(B, C) * d(lnw) + d(lnb)
+    rkrk = (rr * kk * d(r_k).reshape(H, 64)).sum(-1, keepdim=True)
+    out = (yn + (rkrk * vv).reshape(B, C)).half().double() * d(gate)
+    dev = [t.contiguous().cuda() for t in vecs]
+    Sd = S_slot.cuda().contiguous()
+    o = torch.empty(B, C, dtype=torch.float16, device="cuda")
+    # keep every device tensor referenced until the kernel has run
+    sl_d, g_d, rk_d, lw_d, lb_d = (t.cuda() for t in (slots, gate, r_k, lnw, lnb))
+    _lib.check(lib.rwkv7_wkv_gn_step(Sd.data_ptr(), sl_d.data_ptr(), *[t.data_ptr() for t in dev],
+                                     g_d.data_ptr(), rk_d.data_ptr(), lw_d.data_ptr(),
+                                     lb_d.data_ptr(), o.data_ptr(), B, H, 0,
+                                     torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert rel_l2(Sd.cpu()[slots.long()], S.float()) < 1e-5
+    assert rel_l2(o.float(), out) < 2e-3
