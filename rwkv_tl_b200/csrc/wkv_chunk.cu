@@ -219,15 +219,26 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src));
 }
 
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool pred) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  const int sz = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(sz));
+}
+
+constexpr int NSTAGE = 4;  // chunk records in flight per CTA
+constexpr size_t SCAN_SMEM = (size_t)NSTAGE * (REC + CL * 8 / 2) * sizeof(float);
+
 // grid = (S, H, 8 row groups), block = 256: warp w owns state row v = 8 * group + w.
-// Chunk records are double-buffered in shared memory with cp.async (the next
-// chunk streams in while this one is processed). y (fp16, rounded like the
-// reference's y store) goes to ybuf [M, C].
+// Chunk records (and the 16 x 8 values of v the CTA needs) stream through an
+// NSTAGE-deep cp.async ring, so each chunk only waits for its own math. y (fp16,
+// rounded like the reference's y store) goes to ybuf [M, C].
 __global__ void __launch_bounds__(256) k_chunk_scan(
     const __half* __restrict__ vbuf, const float* __restrict__ rec, const int* __restrict__ cu,
     const int* __restrict__ chunk_cu, const int* __restrict__ slots, float* __restrict__ rnn,
     __half* __restrict__ ybuf, int C) {
-  __shared__ __align__(16) float Rb[2][REC];
+  extern __shared__ __align__(16) float scan_smem[];
+  float* Rb = scan_smem;                                                   // [NSTAGE][REC]
+  __half* Vb = reinterpret_cast<__half*>(scan_smem + (size_t)NSTAGE * REC);  // [NSTAGE][CL][8]
   const int s = blockIdx.x, h = blockIdx.y, H = gridDim.y, grp = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = grp * 8 + warp;
@@ -236,32 +247,29 @@ __global__ void __launch_bounds__(256) k_chunk_scan(
   float2 st = *reinterpret_cast<const float2*>(Srow + 2 * lane);
   const int c0 = chunk_cu[s], c1 = chunk_cu[s + 1];
   const int m_beg = cu[s], m_end = cu[s + 1];
-  auto stage = [&](int buf, int c) {
-    const float* src = rec + ((size_t)c * H + h) * REC;
-    for (int i = tid; i < REC / 4; i += 256) cp_async16(&Rb[buf][4 * i], src + 4 * i);
-  };
-  auto load_v = [&](int c) {
-    const int m0 = m_beg + (c - c0) * CL;
-    const int n = min(CL, m_end - m0);
-    return lane < n ? h2f(vbuf[(size_t)(m0 + lane) * C + h * KD + row]) : 0.f;
-  };
-  float vnext = 0.f;
-  if (c0 < c1) {
-    stage(0, c0);
-    vnext = load_v(c0);
-  }
-  asm volatile("cp.async.commit_group;\n" ::);
-  for (int c = c0; c < c1; ++c) {
-    const int buf = (c - c0) & 1;
-    const float vt = vnext;
-    if (c + 1 < c1) {
-      stage(buf ^ 1, c + 1);
-      vnext = load_v(c + 1);
+  auto stage = [&](int c) {
+    if (c < c1) {
+      const int buf = (c - c0) % NSTAGE;
+      const float* src = rec + ((size_t)c * H + h) * REC;
+      for (int i = tid; i < REC / 4; i += 256) cp_async16(Rb + (size_t)buf * REC + 4 * i, src + 4 * i);
+      if (tid < CL) {  // token tid's 8 values of v for this CTA's rows (zero past the end)
+        const int m = m_beg + (c - c0) * CL + tid;
+        const bool ok = m < m_end;
+        cp_async16_zfill(Vb + ((size_t)buf * CL + tid) * 8,
+                         vbuf + (size_t)(ok ? m : m_beg) * C + h * KD + grp * 8, ok);
+      }
     }
     asm volatile("cp.async.commit_group;\n" ::);
-    asm volatile("cp.async.wait_group 1;\n" ::);
-    __syncthreads();
-    const float* R = Rb[buf];
+  };
+#pragma unroll
+  for (int i = 0; i < NSTAGE - 1; ++i) stage(c0 + i);
+  for (int c = c0; c < c1; ++c) {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(NSTAGE - 2));
+    __syncthreads();  // chunk c landed; every warp is done with chunk c - 1's buffer
+    stage(c + NSTAGE - 1);
+    const int buf = (c - c0) % NSTAGE;
+    const float* R = Rb + (size_t)buf * REC;
+    const float vt = lane < CL ? __half2float(Vb[((size_t)buf * CL + lane) * 8 + warp]) : 0.f;
     const int m0 = m_beg + (c - c0) * CL;
     const int n = min(CL, m_end - m0);
     float pw[16], pq[16];
@@ -272,29 +280,37 @@ __global__ void __launch_bounds__(256) k_chunk_scan(
       pw[t] = w2.x * st.x + w2.y * st.y;
       pq[t] = q2.x * st.x + q2.y * st.y;
     }
-    float sa = reduce16(pw, lane);
-    float y = reduce16(pq, lane);
-    const int tt = (lane >> 1) & 15;
+    // the P_U v / P_Y v terms join the partial sums before the reduction: lane j < 16
+    // holds v_j and adds column j of P_U / P_Y to every row's partial
 #pragma unroll
-    for (int j = 0; j < CL; ++j) {
-      const float vj = __shfl_sync(0xffffffffu, vt, j);
-      sa += R[OFF_PU + tt * CL + j] * vj;
-      y += R[OFF_PY + tt * CL + j] * vj;
+    for (int t = 0; t < CL; ++t) {
+      if (lane < CL) {
+        pw[t] += R[OFF_PU + t * CL + lane] * vt;
+        pq[t] += R[OFF_PY + t * CL + lane] * vt;
+      }
     }
+    const float sa = reduce16(pw, lane);
+    const float y = reduce16(pq, lane);
+    const int tt = (lane >> 1) & 15;
     if ((lane & 1) == 0 && tt < n) ybuf[(size_t)(m0 + tt) * C + h * KD + row] = f2h(y);
     const float2 gl = *reinterpret_cast<const float2*>(R + OFF_G + 2 * lane);
-    float2 ns = make_float2(st.x * gl.x, st.y * gl.y);
+    float2 n0 = make_float2(st.x * gl.x, st.y * gl.y), n1 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int j = 0; j < CL; ++j) {
-      const float saj = __shfl_sync(0xffffffffu, sa, 2 * j);
-      const float vj = __shfl_sync(0xffffffffu, vt, j);
-      const float2 b2 = *reinterpret_cast<const float2*>(R + OFF_B + j * KD + 2 * lane);
-      const float2 k2 = *reinterpret_cast<const float2*>(R + OFF_K + j * KD + 2 * lane);
-      ns.x += saj * b2.x + vj * k2.x;
-      ns.y += saj * b2.y + vj * k2.y;
+    for (int j = 0; j < CL; j += 2) {
+      const float sa0 = __shfl_sync(0xffffffffu, sa, 2 * j);
+      const float sa1 = __shfl_sync(0xffffffffu, sa, 2 * j + 2);
+      const float v0 = __shfl_sync(0xffffffffu, vt, j);
+      const float v1 = __shfl_sync(0xffffffffu, vt, j + 1);
+      const float2 b0 = *reinterpret_cast<const float2*>(R + OFF_B + j * KD + 2 * lane);
+      const float2 k0 = *reinterpret_cast<const float2*>(R + OFF_K + j * KD + 2 * lane);
+      const float2 b1 = *reinterpret_cast<const float2*>(R + OFF_B + (j + 1) * KD + 2 * lane);
+      const float2 k1 = *reinterpret_cast<const float2*>(R + OFF_K + (j + 1) * KD + 2 * lane);
+      n0.x += sa0 * b0.x + v0 * k0.x;
+      n0.y += sa0 * b0.y + v0 * k0.y;
+      n1.x += sa1 * b1.x + v1 * k1.x;
+      n1.y += sa1 * b1.y + v1 * k1.y;
     }
-    st = ns;
-    __syncthreads();  // buffer `buf` is restaged two iterations from now
+    st = make_float2(n0.x + n1.x, n0.y + n1.y);
   }
   asm volatile("cp.async.wait_group 0;\n" ::);
   *reinterpret_cast<float2*>(Srow + 2 * lane) = st;
@@ -353,7 +369,20 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   if (rc) return rc;
   k_chunk_prep<<<dim3(M / CL + S, H), 256, 0, st>>>(r, w, k, a, b, cu, chunk_cu, S, C, rec);
   if ((rc = rwkv_check_launch("chunk_prep"))) return rc;
-  k_chunk_scan<<<dim3(S, H, KD / 8), 256, 0, st>>>(v, rec, cu, chunk_cu, slots, rnn, ybuf, C);
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_chunk_scan, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SCAN_SMEM);
+    if (e != cudaSuccess) {
+      rwkv_set_error("chunk_scan: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return RWKV_ERR_CUDA;
+    }
+    attr_done[dev] = true;
+  }
+  k_chunk_scan<<<dim3(S, H, KD / 8), 256, SCAN_SMEM, st>>>(v, rec, cu, chunk_cu, slots, rnn, ybuf,
+                                                          C);
   return rwkv_check_launch("chunk_scan");
 }
 
