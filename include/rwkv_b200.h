@@ -55,7 +55,14 @@ enum { RWKV_SEM_DECODE = 0, RWKV_SEM_PREFILL = 1 };
 enum {
   RWKV_EPI_STORE = 0,  /* C = fp16(acc)                                  */
   RWKV_EPI_RESID = 1,  /* C = fp16(R + fp16(acc))          (x0 + y @ W)  */
-  RWKV_EPI_RELUSQ = 2  /* C = fp16(relu(fp16(acc))^2)      (FFN key)     */
+  RWKV_EPI_RELUSQ = 2, /* C = fp16(relu(fp16(acc))^2)      (FFN key)     */
+  RWKV_EPI_STORE_F32 = 3, /* C = acc as fp32 (C is float*, ldc in floats)   */
+  RWKV_EPI_LORA_ACT = 4,  /* LoRA-down of a 4-problem group v, w, a, g: C =
+                             fp16(act(fp16(acc))), act = tanh for problem 1
+                             (w), sigmoid for problem 3 (g), identity else  */
+  RWKV_EPI_LORA_ACT2 = 5  /* as LORA_ACT, and the fp16 remainder act - hi of
+                             problems 1 / 3 is written 64 / 128 columns to the
+                             right, so hi + lo carries the fp32 activation   */
 };
 
 /* Per-layer weights (device pointers, fp16). C = n_embd, H = C/64. */
@@ -74,6 +81,8 @@ typedef struct rwkv7_layer {
   const void* ffn_x_k;    /* [C]                                                   */
   const void* w_fk;       /* [4C, C] FFN key                                       */
   const void* w_fv;       /* [C, 4C] FFN value                                     */
+  const void* w_lora_up_t; /* [C, 512] K-major LoRA up for the tensor-core path:
+                              v2^T | 0 (32 each) | w2^T | w2^T | a2^T | g2^T | g2^T */
 } rwkv7_layer;
 
 typedef struct rwkv7_model {

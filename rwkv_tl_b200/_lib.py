@@ -50,7 +50,7 @@ class Layer(C.Structure):
         for n in (
             "ln1_w", "ln1_b", "ln2_w", "ln2_b", "mix6", "w_rkv", "w_lora_dn", "w_lora_up",
             "w0", "a0", "v0", "k_k", "k_a", "r_k", "lnx_w", "lnx_b", "w_o", "ffn_x_k",
-            "w_fk", "w_fv",
+            "w_fk", "w_fv", "w_lora_up_t",
         )
     ]
 

@@ -54,10 +54,9 @@ int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __ha
                    __half* out, int n, int C, cudaStream_t st);
 int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,
                            int S, int L, int n_slots, int C, cudaStream_t st);
-int launch_gates(int sem, const __half* ranks, const __half* w_up, const __half* rkv,
-                 const __half* w0, const __half* a0, const __half* v0, const __half* k_k,
-                 const __half* k_a, __half* vfirst, __half* gout, int M, int C, int layer0,
-                 cudaStream_t st);
+int launch_gates_ew(int sem, const void* lora, const __half* rkv, const __half* w0,
+                    const __half* a0, const __half* v0, const __half* k_k, const __half* k_a,
+                    __half* vfirst, __half* gout, int M, int C, int layer0, cudaStream_t st);
 int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t plane,
                       const __half* r_k, const __half* lnx_w, const __half* lnx_b, float* rnn,
                       const int* cu, const int* slots, __half* yg, int n_seqs, int H, int C,
@@ -87,8 +86,13 @@ struct Carve {
   }
 };
 
+// rank buffer columns: v(32) | 0(32) | w hi(64) | w lo(64) | a(64) | g hi(128) | g lo(128);
+// the lo parts carry fp32 activations exactly for the decode semantics (zero for prefill)
+constexpr int RANKS_LD = 512;
+
 struct Work {
   __half *x, *x1, *xmix, *rkv, *ranks, *gbuf, *vfirst, *yg, *xk, *h, *xlast, *lnout;
+  void* lora;  // 4 x [M, C] LoRA up outputs (fp32 decode semantics, fp16 prefill)
   float* chunk_rec;
   int* chunk_cu;
   float* splitk;       // split-K partial tiles for small-M GEMMs
@@ -115,7 +119,8 @@ Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) 
   w.x1 = c.take<__half>(MC);
   w.xmix = c.take<__half>(6 * MC);
   w.rkv = c.take<__half>(3 * MC);
-  w.ranks = c.take<__half>((size_t)M * RWKV_RANK_SUM);
+  w.ranks = c.take<__half>((size_t)M * RANKS_LD);
+  w.lora = c.take<float>(4 * MC);
   w.gbuf = c.take<__half>(6 * MC);
   w.vfirst = c.take<__half>(MC);
   w.yg = c.take<__half>(MC);
@@ -132,7 +137,7 @@ Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) 
 }
 
 int check_model(const rwkv7_model* m) {
-  if (!m || !m->layers || !m->emb || !m->head || m->n_layer <= 0) {
+  if (!m || !m->layers || !m->emb || !m->head || m->n_layer <= 0 || !m->layers[0].w_lora_up_t) {
     rwkv_set_error("rwkv7_model: null pointer or no layers");
     return RWKV_ERR_ARG;
   }
@@ -207,6 +212,9 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const int ns = state->n_slots;
   const __half* emb = (const __half*)model->emb;
   const bool chunked = use_chunked_wkv(M, S);
+  // columns 32..63 of the rank buffer (the zero padding of rank v) must read as zero
+  if (cudaMemsetAsync(w.ranks, 0, (size_t)M * RANKS_LD * sizeof(__half), st) != cudaSuccess)
+    return rwkv_check_launch("ranks memset");
 
   for (int l = 0; l < L; ++l) {
     const rwkv7_layer& Lw = model->layers[l];
@@ -231,18 +239,35 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
       TRY(gemm_launch_ws(p, 3, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
     }
     {
-      // LoRA down-projections into ranks [M, 288] = v(32) | w(64) | a(64) | g(128)
-      const int R = RWKV_RANK_SUM;
+      // LoRA down-projections into the rank buffer: v, tanh(w), a, sigmoid(g), activations
+      // applied on the fp16-rounded GEMM outputs (decode: fp32 activation as hi + lo)
+      const int R = RANKS_LD;
       rwkv7_gemm_problem p[4] = {
           {w.xmix + 3 * MC, wdn + 0 * C, w.ranks + 0, nullptr, M, 32, C, C, C, R},
-          {w.xmix + 1 * MC, wdn + 32 * C, w.ranks + 32, nullptr, M, 64, C, C, C, R},
-          {w.xmix + 4 * MC, wdn + 96 * C, w.ranks + 96, nullptr, M, 64, C, C, C, R},
-          {w.xmix + 5 * MC, wdn + 160 * C, w.ranks + 160, nullptr, M, 128, C, C, C, R}};
-      TRY(gemm_launch_ws(p, 4, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
+          {w.xmix + 1 * MC, wdn + 32 * C, w.ranks + 64, nullptr, M, 64, C, C, C, R},
+          {w.xmix + 4 * MC, wdn + 96 * C, w.ranks + 192, nullptr, M, 64, C, C, C, R},
+          {w.xmix + 5 * MC, wdn + 160 * C, w.ranks + 256, nullptr, M, 128, C, C, C, R}};
+      TRY(gemm_launch_ws(p, 4, sem == SEM_DECODE ? RWKV_EPI_LORA_ACT2 : RWKV_EPI_LORA_ACT,
+                         w.splitk, w.splitk_floats, st));
     }
-    TRY(launch_gates(sem, w.ranks, (const __half*)Lw.w_lora_up, w.rkv, (const __half*)Lw.w0,
-                     (const __half*)Lw.a0, (const __half*)Lw.v0, (const __half*)Lw.k_k,
-                     (const __half*)Lw.k_a, w.vfirst, w.gbuf, M, C, l == 0, st));
+    {
+      // LoRA up-projections on tensor cores: v12, w12, a12, g12 [M, C]
+      const int R = RANKS_LD;
+      const __half* up = (const __half*)Lw.w_lora_up_t;
+      const bool f32 = sem == SEM_DECODE;
+      const size_t esz = f32 ? 4 : 2;
+      char* lo = (char*)w.lora;
+      rwkv7_gemm_problem p[4] = {
+          {w.ranks + 0, up + 0, lo + 0 * MC * esz, nullptr, M, C, 64, R, R, C},
+          {w.ranks + 64, up + 64, lo + 1 * MC * esz, nullptr, M, C, 128, R, R, C},
+          {w.ranks + 192, up + 192, lo + 2 * MC * esz, nullptr, M, C, 64, R, R, C},
+          {w.ranks + 256, up + 256, lo + 3 * MC * esz, nullptr, M, C, 256, R, R, C}};
+      TRY(gemm_launch_ws(p, 4, f32 ? RWKV_EPI_STORE_F32 : RWKV_EPI_STORE, w.splitk,
+                         w.splitk_floats, st));
+    }
+    TRY(launch_gates_ew(sem, w.lora, w.rkv, (const __half*)Lw.w0, (const __half*)Lw.a0,
+                        (const __half*)Lw.v0, (const __half*)Lw.k_k, (const __half*)Lw.k_a,
+                        w.vfirst, w.gbuf, M, C, l == 0, st));
     if (chunked) {
       // gbuf planes: 0 w, 1 k, 2 v, 3 A (k_hat), 4 B; r from the rkv buffer
       TRY(launch_wkv_chunked(w.rkv, w.gbuf, w.gbuf + MC, w.gbuf + 2 * MC, w.gbuf + 3 * MC,

@@ -43,6 +43,45 @@ __device__ __forceinline__ void store_h4(__half* p, float4 v) {
   *reinterpret_cast<uint2*>(p) = u;
 }
 
+// GEMM epilogue for one output pair (c0, c1) at element offset o of C; `prob` is the
+// index of the problem in a grouped launch (RWKV_EPI_LORA_ACT: 1 -> tanh, 3 -> sigmoid).
+template <int EPI>
+__device__ __forceinline__ void epi_store2(void* C, size_t o, float c0, float c1,
+                                           const __half* R, int prob) {
+  if (EPI == RWKV_EPI_STORE_F32) {
+    *reinterpret_cast<float2*>(static_cast<float*>(C) + o) = make_float2(c0, c1);
+    return;
+  }
+  __half2 h;
+  if (EPI == RWKV_EPI_STORE) {
+    h = __floats2half2_rn(c0, c1);
+  } else if (EPI == RWKV_EPI_RESID) {
+    const float2 r = __half22float2(*reinterpret_cast<const __half2*>(R + o));
+    h = __floats2half2_rn(r.x + r16(c0), r.y + r16(c1));
+  } else if (EPI == RWKV_EPI_RELUSQ) {
+    const float h0 = fmaxf(r16(c0), 0.f), h1 = fmaxf(r16(c1), 0.f);
+    h = __floats2half2_rn(h0 * h0, h1 * h1);
+  } else {  // RWKV_EPI_LORA_ACT / RWKV_EPI_LORA_ACT2
+    float a = r16(c0), b = r16(c1);
+    if (prob == 1) {
+      a = tanhf(a);
+      b = tanhf(b);
+    } else if (prob == 3) {
+      a = 1.0f / (1.0f + expf(-a));
+      b = 1.0f / (1.0f + expf(-b));
+    }
+    h = __floats2half2_rn(a, b);
+    if (EPI == RWKV_EPI_LORA_ACT2 && (prob == 1 || prob == 3)) {
+      // fp32 activation kept as fp16 hi + lo: lo goes `lo_off` columns to the right
+      const int lo_off = prob == 1 ? 64 : 128;
+      const float2 hf = __half22float2(h);
+      *reinterpret_cast<__half2*>(static_cast<__half*>(C) + o + lo_off) =
+          __floats2half2_rn(a - hf.x, b - hf.y);
+    }
+  }
+  *reinterpret_cast<__half2*>(static_cast<__half*>(C) + o) = h;
+}
+
 // Block-wide sum of NV floats; `red` needs 32*NV floats of shared memory.
 template <int NV>
 __device__ __forceinline__ void block_sum(float (&v)[NV], float* red) {

@@ -53,18 +53,6 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 }
 
 template <int EPI>
-__device__ __forceinline__ __half2 epilogue(float c0, float c1, const __half* R, size_t ro) {
-  if (EPI == RWKV_EPI_STORE) return __floats2half2_rn(c0, c1);
-  if (EPI == RWKV_EPI_RESID) {
-    const float2 r = __half22float2(*reinterpret_cast<const __half2*>(R + ro));
-    return __floats2half2_rn(r.x + r16(c0), r.y + r16(c1));
-  }
-  // RELUSQ
-  const float h0 = fmaxf(r16(c0), 0.f), h1 = fmaxf(r16(c1), 0.f);
-  return __floats2half2_rn(h0 * h0, h1 * h1);
-}
-
-template <int EPI>
 __global__ void __launch_bounds__(NTHREADS) k_gemm_mma(const GemmGroup grp) {
   extern __shared__ __align__(128) __half smem[];
   if ((int)blockIdx.z >= grp.n) return;
@@ -141,7 +129,6 @@ __global__ void __launch_bounds__(NTHREADS) k_gemm_mma(const GemmGroup grp) {
   }
   cp_wait<0>();
 
-  __half* Cp = static_cast<__half*>(P.C);
   const __half* R = static_cast<const __half*>(P.R);
 #pragma unroll
   for (int mi = 0; mi < 4; ++mi) {
@@ -154,8 +141,7 @@ __global__ void __launch_bounds__(NTHREADS) k_gemm_mma(const GemmGroup grp) {
         const int row = m0 + wm * 64 + mi * 16 + (lane >> 2) + hh * 8;
         if (row >= P.M) continue;
         const size_t o = (size_t)row * P.ldc + col;
-        *reinterpret_cast<__half2*>(Cp + o) =
-            epilogue<EPI>(acc[mi][ni][2 * hh], acc[mi][ni][2 * hh + 1], R, o);
+        epi_store2<EPI>(P.C, o, acc[mi][ni][2 * hh], acc[mi][ni][2 * hh + 1], R, blockIdx.z);
       }
     }
   }
@@ -195,7 +181,7 @@ int gemm_validate(const rwkv7_gemm_problem* p, int n) {
   for (int i = 0; i < n; ++i) {
     const rwkv7_gemm_problem& q = p[i];
     if (q.M < 0 || q.N < 0 || q.K <= 0 || q.K % BK || q.N % 2 || q.lda % 8 || q.ldb % 8 ||
-        q.ldc % 2 || !q.A || !q.B || !q.C || q.lda < q.K || q.ldb < q.K || q.ldc < q.N) {
+        q.ldc % 2 || !q.A || !q.B || !q.C || (reinterpret_cast<uintptr_t>(q.C) & 7) || q.lda < q.K || q.ldb < q.K || q.ldc < q.N) {
       rwkv_set_error("rwkv7_gemm_f16: bad problem %d (M=%d N=%d K=%d lda=%d ldb=%d ldc=%d)", i,
                      q.M, q.N, q.K, q.lda, q.ldb, q.ldc);
       return RWKV_ERR_ARG;
@@ -216,6 +202,9 @@ int gemm_mma_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStre
     case RWKV_EPI_STORE: return launch_group<RWKV_EPI_STORE>(g, st);
     case RWKV_EPI_RESID: return launch_group<RWKV_EPI_RESID>(g, st);
     case RWKV_EPI_RELUSQ: return launch_group<RWKV_EPI_RELUSQ>(g, st);
+    case RWKV_EPI_STORE_F32: return launch_group<RWKV_EPI_STORE_F32>(g, st);
+    case RWKV_EPI_LORA_ACT: return launch_group<RWKV_EPI_LORA_ACT>(g, st);
+    case RWKV_EPI_LORA_ACT2: return launch_group<RWKV_EPI_LORA_ACT2>(g, st);
   }
   rwkv_set_error("rwkv7_gemm_f16: unknown epilogue %d", epi);
   return RWKV_ERR_ARG;

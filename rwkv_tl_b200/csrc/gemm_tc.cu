@@ -141,37 +141,26 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Apply the epilogue to 16 consecutive columns of one output row and store.
 template <int EPI>
-__device__ __forceinline__ __half2 epi2(float c0, float c1, const __half* R, size_t o) {
-  if (EPI == RWKV_EPI_STORE) return __floats2half2_rn(c0, c1);
-  if (EPI == RWKV_EPI_RESID) {
-    const float2 r = __half22float2(*reinterpret_cast<const __half2*>(R + o));
-    return __floats2half2_rn(r.x + r16(c0), r.y + r16(c1));
-  }
-  const float h0 = fmaxf(r16(c0), 0.f), h1 = fmaxf(r16(c1), 0.f);
-  return __floats2half2_rn(h0 * h0, h1 * h1);
-}
-
-// Apply the epilogue to 16 consecutive columns of one output row and store fp16.
-template <int EPI>
-__device__ __forceinline__ void store16(const float (&v)[16], __half* C, const __half* R, int row,
-                                        int col, int N, int ldc, bool vec) {
+__device__ __forceinline__ void store16(const float (&v)[16], void* Cv, const __half* R, int row,
+                                        int col, int N, int ldc, bool vec, int prob) {
   const size_t o = (size_t)row * ldc + col;
-  if (col + 16 <= N) {
+  if (EPI != RWKV_EPI_STORE_F32 && EPI != RWKV_EPI_LORA_ACT2 && col + 16 <= N && vec) {
+    __half* C = static_cast<__half*>(Cv);
     uint4 pk[2];
     __half2* h2 = reinterpret_cast<__half2*>(pk);
+    __half tmp[2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) h2[i] = epi2<EPI>(v[2 * i], v[2 * i + 1], R, o + 2 * i);
-    if (vec) {
-      reinterpret_cast<uint4*>(C + o)[0] = pk[0];
-      reinterpret_cast<uint4*>(C + o)[1] = pk[1];
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) reinterpret_cast<__half2*>(C + o)[i] = h2[i];
+    for (int i = 0; i < 8; ++i) {
+      epi_store2<EPI>(tmp, 0, v[2 * i], v[2 * i + 1], R + o + 2 * i, prob);
+      h2[i] = *reinterpret_cast<__half2*>(tmp);
     }
+    reinterpret_cast<uint4*>(C + o)[0] = pk[0];
+    reinterpret_cast<uint4*>(C + o)[1] = pk[1];
   } else {
     for (int i = 0; i + 1 < 16 && col + i < N; i += 2)
-      *reinterpret_cast<__half2*>(C + o + i) = epi2<EPI>(v[i], v[i + 1], R, o + i);
+      epi_store2<EPI>(Cv, o + i, v[i], v[i + 1], R, prob);
   }
 }
 
@@ -270,7 +259,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int row = m0 + quad * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-    __half* C = static_cast<__half*>(P.C);
+    void* C = P.C;
     const __half* R = static_cast<const __half*>(P.R);
     const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
     const bool all_ok = __all_sync(0xffffffffu, ok);
@@ -281,7 +270,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
           float v[16];
           tmem_ld16(trow + c0, v);  // all lanes execute (sync.aligned)
           const int col = n0 + c0;
-          if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec);
+          if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec, g);
         }
       }
     } else {
@@ -336,12 +325,10 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ R
     const float4 q = __ldcg(reinterpret_cast<const float4*>(P.ws + s * MN + i));
     acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
   }
-  __half* C = static_cast<__half*>(P.C);
   const __half* R = static_cast<const __half*>(P.R);
   const size_t o = (size_t)row * P.ldc + col;
-  const __half2 h0 = epi2<EPI>(acc.x, acc.y, R, o), h1 = epi2<EPI>(acc.z, acc.w, R, o + 2);
-  reinterpret_cast<__half2*>(C + o)[0] = h0;
-  reinterpret_cast<__half2*>(C + o)[1] = h1;
+  epi_store2<EPI>(P.C, o, acc.x, acc.y, R, blockIdx.y);
+  epi_store2<EPI>(P.C, o + 2, acc.z, acc.w, R, blockIdx.y);
 }
 
 // ---------------------------------------------------------------------------
@@ -448,7 +435,7 @@ bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n) {
     if (p[i].K % BK || p[i].lda % 8 || p[i].ldb % 8 || p[i].M <= 0 || p[i].N <= 0) return false;
     if ((reinterpret_cast<uintptr_t>(p[i].A) | reinterpret_cast<uintptr_t>(p[i].B)) & 15)
       return false;
-    if ((reinterpret_cast<uintptr_t>(p[i].C) | reinterpret_cast<uintptr_t>(p[i].R)) & 3) return false;
+    if ((reinterpret_cast<uintptr_t>(p[i].C) | reinterpret_cast<uintptr_t>(p[i].R)) & 7) return false;
   }
   return true;
 }
@@ -515,7 +502,10 @@ int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, 
   switch (epi) {
     case RWKV_EPI_STORE: rc = launch_tc<BN, RWKV_EPI_STORE, STAGES>(prm, grid, st); break;
     case RWKV_EPI_RESID: rc = launch_tc<BN, RWKV_EPI_RESID, STAGES>(prm, grid, st); break;
-    default: rc = launch_tc<BN, RWKV_EPI_RELUSQ, STAGES>(prm, grid, st); break;
+    case RWKV_EPI_RELUSQ: rc = launch_tc<BN, RWKV_EPI_RELUSQ, STAGES>(prm, grid, st); break;
+    case RWKV_EPI_STORE_F32: rc = launch_tc<BN, RWKV_EPI_STORE_F32, STAGES>(prm, grid, st); break;
+    case RWKV_EPI_LORA_ACT: rc = launch_tc<BN, RWKV_EPI_LORA_ACT, STAGES>(prm, grid, st); break;
+    default: rc = launch_tc<BN, RWKV_EPI_LORA_ACT2, STAGES>(prm, grid, st); break;
   }
   if (rc || splits == 1) return rc;
   ReduceParams rp;
@@ -530,7 +520,10 @@ int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, 
   switch (epi) {
     case RWKV_EPI_STORE: k_splitk_reduce<RWKV_EPI_STORE><<<rgrid, 256, 0, st>>>(rp); break;
     case RWKV_EPI_RESID: k_splitk_reduce<RWKV_EPI_RESID><<<rgrid, 256, 0, st>>>(rp); break;
-    default: k_splitk_reduce<RWKV_EPI_RELUSQ><<<rgrid, 256, 0, st>>>(rp); break;
+    case RWKV_EPI_RELUSQ: k_splitk_reduce<RWKV_EPI_RELUSQ><<<rgrid, 256, 0, st>>>(rp); break;
+    case RWKV_EPI_STORE_F32: k_splitk_reduce<RWKV_EPI_STORE_F32><<<rgrid, 256, 0, st>>>(rp); break;
+    case RWKV_EPI_LORA_ACT: k_splitk_reduce<RWKV_EPI_LORA_ACT><<<rgrid, 256, 0, st>>>(rp); break;
+    default: k_splitk_reduce<RWKV_EPI_LORA_ACT2><<<rgrid, 256, 0, st>>>(rp); break;
   }
   return rwkv_check_launch("splitk_reduce");
 }

@@ -10,7 +10,9 @@ packs per layer:
 
 * ``w_rkv [3C, C]`` = receptance | key | value;
 * ``w_lora_dn [288, C]`` = v1^T | w1^T | a1^T | g1^T (LoRA down, ranks 32/64/64/128);
-* ``w_lora_up [288, C]`` = v2 | w2 | a2 | g2 (LoRA up, ``[r, C]`` as stored);
+* ``w_lora_up [288, C]`` = v2 | w2 | a2 | g2 (LoRA up, ``[r, C]`` as stored) and its
+  K-major copy ``w_lora_up_t [C, 512]`` (v padded to 64, w and g repeated for the
+  hi + lo activation split) for the tensor-core GEMM;
 * ``mix6 [6, C]`` = x_r | x_w | x_k | x_v | x_a | x_g.
 
 Weight preparation runs once at load with plain torch ops; only the forward
@@ -86,6 +88,12 @@ class RWKV7Weight:
                 "w_fk": W[f"{p}.ffn.key.weight"].contiguous(),
                 "w_fv": W[f"{p}.ffn.value.weight"].contiguous(),
             }
+            # K-major LoRA up for the tensor-core GEMM: v padded from rank 32 to 64, w and g
+            # repeated so that an activation carried as fp16 hi + lo is applied exactly
+            zeros = torch.zeros(C, 32, dtype=dtype, device=dev)
+            w2t, g2t = W[f"{a}.w2"].t(), W[f"{a}.g2"].t()
+            lay["w_lora_up_t"] = torch.cat(
+                [W[f"{a}.v2"].t(), zeros, w2t, w2t, W[f"{a}.a2"].t(), g2t, g2t], 1).contiguous()
             self.layers.append(lay)
         self._cmodel: _lib.Model | None = None
 
