@@ -125,13 +125,9 @@ def barrier(world):
 
 
 def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
+    from rwkv_tl_b200.shard import max_over_ranks as _max
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return _max(x, device="cuda") if world > 1 else x
 
 
 # --------------------------------------------------------------------------- #

@@ -1,8 +1,8 @@
 // Gate math + per-head L2 norm on the LoRA up-projection outputs.
 //
 // The up-projections themselves run as one grouped tcgen05 GEMM (gemm_tc.cu) over
-// the padded rank buffer [M, 320] = v(32, zero-padded to 64) | tanh(w)(64) | a(64) |
-// sigmoid(g)(128) and the K-major weights w_lora_up_t [C, 320], giving v12, w12, a12,
+// the padded rank buffer [M, 512] = v(32, zero-padded to 64) | tanh(w) hi, lo (64 + 64) | a(64) |
+// sigmoid(g) hi, lo (128 + 128) and the K-major weights w_lora_up_t [C, 512], giving v12, w12, a12,
 // g12 [M, C] (fp32 with decode rounding semantics, fp16 with prefill semantics).
 // This kernel finishes the gates.
 //
