@@ -23,7 +23,8 @@ INCLUDE = PKG.parent / "include"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
-         "-Xptxas", "-v" if os.environ.get("RWKV_PTXAS_VERBOSE") else "-O3"]
+         "-Xptxas", "-v" if os.environ.get("RWKV_PTXAS_VERBOSE") else "-O3",
+         *os.environ.get("RWKV_B200_NVCC_EXTRA", "").split()]
 
 
 def nvcc() -> str:

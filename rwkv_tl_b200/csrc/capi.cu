@@ -36,7 +36,11 @@ int rwkv_check_launch(const char* what) {
 extern "C" const char* rwkv_b200_last_error(void) { return g_err; }
 extern "C" int rwkv_b200_abi_version(void) { return RWKV_B200_ABI_VERSION; }
 int gemm_tc_timeout_flag();
-extern "C" int rwkv_b200_device_error(void) { return gemm_tc_timeout_flag(); }
+int decode_persist_timeout_flag();
+extern "C" int rwkv_b200_device_error(void) {
+  const int a = gemm_tc_timeout_flag(), b = decode_persist_timeout_flag();
+  return a | (b << 1);
+}
 
 extern "C" unsigned long long rwkv_b200_launch_count(void) {
   return __atomic_load_n(&g_launches, __ATOMIC_RELAXED);

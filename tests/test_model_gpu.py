@@ -211,12 +211,14 @@ def test_chunked_wkv_matches_serial(monkeypatch, lens):
     assert (a.cmix_x.float() - b.cmix_x.float()).abs().max() < 1e-2
 
 
-@pytest.mark.parametrize("B", [1, 3, 8])
-@pytest.mark.parametrize("mode", ["gemv", "token"])
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("mode", ["persist", "gemv", "token"])
 def test_small_batch_decode_paths(monkeypatch, B, mode):
-    """Small-batch decode (fused GEMV kernels, or the token-batch kernels) from random
-    states vs the oracle, at a width the GEMV path takes (C=768)."""
-    monkeypatch.setenv("RWKV_B200_DECODE", mode)
+    """Small-batch decode from random states vs the oracle, at a width the GEMV paths
+    take (C=768): the persistent single-kernel step (B <= 4), the three-kernel PDL
+    chain, and the token-batch kernels."""
+    monkeypatch.setenv("RWKV_B200_DECODE", "token" if mode == "token" else "gemv")
+    monkeypatch.setenv("RWKV_B200_DECODE_PERSIST", "1" if mode == "persist" else "0")
     m, o = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 4)
     bs = BatchedState(m.L, m.C, B + 2, device="cuda")
     g = torch.Generator(device="cuda").manual_seed(11 + B)
