@@ -60,6 +60,7 @@ constexpr int PMAXL = 24;
 constexpr int MAXG = 160;  // CTAs (SMs) at most
 constexpr int RA = 24;     // phase-A rows per task (multiple of 8)
 constexpr int FROWS = 32;  // FFN hidden rows per CTA at most (groups of 8)
+constexpr int NREP = 4;    // replicas of the FFN accumulator (CTA c adds into c % NREP)
 constexpr uint64_t WAIT_NS = 200000000ull;
 
 struct GridBar {
@@ -104,8 +105,8 @@ struct PParams {
   const int* slots;
   const __half *emb, *head, *lnout_w, *lnout_b;
   __half* logits;
-  __half *xres, *x1, *xln1, *xln2, *rkv, *ranks, *vfirst;
-  float* acc;  // [L][2][B][C]
+  __half *xln1, *xln2, *rkv, *ranks, *vfirst;
+  float* acc;  // per layer: acc1 [B][C], then acc2 [NREP][B][C]
   GridBar* bar;
   float* rnn;
   __half *tmix_x, *cmix_x;
@@ -116,7 +117,7 @@ struct PParams {
 };
 
 struct SmemLayout {
-  size_t a, ac, bv, bc, k, cc, xc, total;
+  size_t a, ac, bv, bc, k, cc, xc, xr, total;
 };
 
 __host__ __device__ inline size_t al1k(size_t v) { return (v + 1023) & ~size_t(1023); }
@@ -133,7 +134,8 @@ __host__ __device__ inline SmemLayout smem_layout(int NB, int C, int rows_b) {
   s.k = al1k(s.bc + 8 * 128);
   s.cc = al1k(s.k + (size_t)FROWS * C * 2);
   s.xc = al1k(s.cc + (size_t)(3 + NB) * C * 2);
-  s.total = al1k(s.xc + (size_t)NB * mld_of(C) * 2);
+  s.xr = al1k(s.xc + (size_t)NB * mld_of(C) * 2);
+  s.total = al1k(s.xr + (size_t)NB * C * 2);
   return s;
 }
 
@@ -336,6 +338,33 @@ __device__ __forceinline__ void gemv32_partial(uint32_t wbase, int R, const __ha
 
 __device__ __forceinline__ float ldcg_h(const __half* p) { return __half2float(__ldcg(p)); }
 
+// Four consecutive fp16 channels <-> floats (8-byte accesses).
+__device__ __forceinline__ void ld4h(const __half* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void st4h(__half* p, const float (&v)[4]) {
+  uint2 u;
+  *reinterpret_cast<__half2*>(&u.x) = __floats2half2_rn(v[0], v[1]);
+  *reinterpret_cast<__half2*>(&u.y) = __floats2half2_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+__device__ __forceinline__ void cp4h(__half* dst, const __half* src) {
+  *reinterpret_cast<uint2*>(dst) = __ldcg(reinterpret_cast<const uint2*>(src));
+}
+// fp16(sum of the NREP accumulator replicas) of four channels, replicas in order.
+__device__ __forceinline__ void ld_acc_rep(const float* a, size_t rep_stride, float (&v)[4]) {
+  float4 s = __ldcg(reinterpret_cast<const float4*>(a));
+#pragma unroll
+  for (int r = 1; r < NREP; ++r) {
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(a + r * rep_stride));
+    s.x += t.x; s.y += t.y; s.z += t.z; s.w += t.w;
+  }
+  v[0] = r16(s.x); v[1] = r16(s.y); v[2] = r16(s.z); v[3] = r16(s.w);
+}
+
 // Per-CTA staging state: one mbarrier per stream, and how many phases of each were
 // issued / consumed (so that an aborting CTA can drain what is still in flight).
 enum { MB_A = 0, MB_B, MB_K, MB_V, MB_H0, MB_H1, MB_H2, MB_N };
@@ -460,6 +489,10 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
   __half* sFk = reinterpret_cast<__half*>(smem + lay.k);
   __half* sCc = reinterpret_cast<__half*>(smem + lay.cc);
   __half* sXc = reinterpret_cast<__half*>(smem + lay.xc);  // [NB][MLD]
+  __half* sXr = reinterpret_cast<__half*>(smem + lay.xr);  // residual stream x [NB][C]
+  constexpr int E = 4;   // element-wise channels per thread: c0 = 4 tid .. + 3
+  const int c0 = 4 * tid;
+  const bool ew = c0 < C;  // threads past C / 4 hold zeros in the LayerNorms
   __half* mix = sFk;                                       // phase A: [6][NB][MLD]
   unsigned char* bscr = smem + lay.a;                      // phase B scratch
   // head tiles (32 rows x C, 64 KB at C = 1024): A rows + A vectors | FFN key rows |
@@ -506,66 +539,67 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
 
   for (int l = 0; l < P.L && alive; ++l) {
     const DecLayer& Lw = P.layers[l];
-    float* acc1 = P.acc + (size_t)(2 * l) * BC;
-    float* acc2 = P.acc + (size_t)(2 * l + 1) * BC;
+    float* acc1 = P.acc + (size_t)l * (1 + NREP) * BC;
+    float* acc2 = acc1 + BC;
     float* rnn = P.rnn + (size_t)l * P.n_slots * H * 4096;
     __half* tmix_x = P.tmix_x + (size_t)l * P.n_slots * C;
     __half* cmix_x = P.cmix_x + (size_t)l * P.n_slots * C;
 
     // =================== phase A ===================
     {
-      float lw[CPL], lb[CPL], mu[6][CPL], x[NB][CPL], prev[NB][CPL];
-      const float* acc2p = P.acc + (size_t)(2 * l - 1) * BC;
+      float lw[E] = {}, lb[E] = {}, mu[6][E] = {}, x[NB][E], prev[NB][E] = {};
+      const float* acc2p = acc1 - (size_t)NREP * BC;  // previous layer's FFN sums
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         const int bb = b < B ? b : 0;
+        if (!ew) {
 #pragma unroll
-        for (int k = 0; k < CPL; ++k) {
-          const int c = tid + NT * k;
-          const size_t o = (size_t)bb * C + c;
-          x[b][k] = l == 0 ? h2f(P.emb[(size_t)s_tok[b] * C + c])
-                           : r16(ldcg_h(P.x1 + o) + r16(__ldcg(acc2p + o)));
+          for (int k = 0; k < E; ++k) x[b][k] = 0.f;
+        } else if (l == 0) {
+          ld4h(P.emb + (size_t)s_tok[b] * C + c0, x[b]);
+        } else {
+          float xr[E], a[E];
+          ld_acc_rep(acc2p + (size_t)bb * C + c0, BC, a);
+          ld4h(sXr + (size_t)bb * C + c0, xr);
+#pragma unroll
+          for (int k = 0; k < E; ++k) x[b][k] = r16(xr[k] + a[k]);
         }
       }
       if (l == 10) STAMP(200);
       if (!stage_wait(S, MB_A, P.bar)) { alive = false; break; }
       if (l == 10) STAMP(201);
+      if (ew) {
+        ld4h(sAc + c0, lw);
+        ld4h(sAc + C + c0, lb);
 #pragma unroll
-      for (int k = 0; k < CPL; ++k) {
-        const int c = tid + NT * k;
-        lw[k] = h2f(sAc[c]);
-        lb[k] = h2f(sAc[C + c]);
+        for (int t = 0; t < 6; ++t) ld4h(sAc + (2 + t) * C + c0, mu[t]);
 #pragma unroll
-        for (int t = 0; t < 6; ++t) mu[t][k] = h2f(sAc[(2 + t) * C + c]);
-#pragma unroll
-        for (int b = 0; b < NB; ++b) prev[b][k] = h2f(sAc[(8 + b) * C + c]);
-      }
-      if (cta == 0) {
-        __half* cmix_prev = l ? P.cmix_x + (size_t)(l - 1) * P.n_slots * C : nullptr;
-        for (int b = 0; b < B; ++b) {
-#pragma unroll
-          for (int k = 0; k < CPL; ++k) {
-            const int c = tid + NT * k;
-            P.xres[(size_t)b * C + c] = f2h(x[b][k]);
-            if (cmix_prev) cmix_prev[(size_t)s_slot[b] * C + c] = __ldcg(P.xln2 + (size_t)b * C + c);
-          }
+        for (int b = 0; b < NB; ++b) {
+          ld4h(sAc + (8 + b) * C + c0, prev[b]);
+          st4h(sXr + (size_t)b * C + c0, x[b]);  // this layer's input, kept for phase C
         }
+        if (cta == 0 && l > 0)  // previous layer's cmix state x (read there by every CTA)
+          for (int b = 0; b < B; ++b)
+            cp4h(P.cmix_x + (size_t)(l - 1) * P.n_slots * C + (size_t)s_slot[b] * C + c0,
+                 P.xln2 + (size_t)b * C + c0);
       }
       if (l == 10) STAMP(203);
-      ln_regs<NB, CPL>(x, lw, lb, C, red);
+      ln_regs<NB, E>(x, lw, lb, C, red);
       if (l == 10) STAMP(204);
       // mixes (lerp.py:106-114: diff in fp16, fused fp16 fma)
+      if (ew) {
 #pragma unroll
-      for (int b = 0; b < NB; ++b)
+        for (int b = 0; b < NB; ++b) {
 #pragma unroll
-        for (int k = 0; k < CPL; ++k) {
-          const int c = tid + NT * k;
-          const float diff = r16(prev[b][k] - x[b][k]);
+          for (int t = 0; t < 6; ++t) {
+            float m[E];
 #pragma unroll
-          for (int t = 0; t < 6; ++t)
-            mix[((size_t)t * NB + b) * MLD + c] = f2h(x[b][k] + mu[t][k] * diff);
-          if (cta == 0 && b < B) P.xln1[(size_t)b * C + c] = f2h(x[b][k]);
+            for (int k = 0; k < E; ++k) m[k] = x[b][k] + mu[t][k] * r16(prev[b][k] - x[b][k]);
+            st4h(mix + ((size_t)t * NB + b) * MLD + c0, m);
+          }
+          if (cta == 0 && b < B) st4h(P.xln1 + (size_t)b * C + c0, x[b]);
         }
+      }
       __syncthreads();
       if (l == 10) STAMP(202);
       if (atask) {  // the task's rows on the tensor cores, k-quarter partials summed in order
@@ -814,40 +848,47 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
     // =================== phase C ===================
     {
       __half* xk = sXc;  // [NB][MLD]
-      float lw[CPL], lb[CPL], mu[CPL], x[NB][CPL], prev[NB][CPL];
+      float lw[E] = {}, lb[E] = {}, mu[E] = {}, x[NB][E], prev[NB][E] = {};
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         const int bb = b < B ? b : 0;
+        if (ew) {
+          float xr[E];
+          const float4 a = __ldcg(reinterpret_cast<const float4*>(acc1 + (size_t)bb * C + c0));
+          ld4h(sXr + (size_t)bb * C + c0, xr);
+          x[b][0] = r16(xr[0] + r16(a.x));
+          x[b][1] = r16(xr[1] + r16(a.y));
+          x[b][2] = r16(xr[2] + r16(a.z));
+          x[b][3] = r16(xr[3] + r16(a.w));
+        } else {
 #pragma unroll
-        for (int k = 0; k < CPL; ++k) {
-          const int c = tid + NT * k;
-          const size_t o = (size_t)bb * C + c;
-          x[b][k] = r16(ldcg_h(P.xres + o) + r16(__ldcg(acc1 + o)));
-          if (cta == 0 && b < B) P.x1[o] = f2h(x[b][k]);
+          for (int k = 0; k < E; ++k) x[b][k] = 0.f;
         }
       }
       if (l == 10) STAMP(151);
       if (!stage_wait(S, MB_K, P.bar)) { alive = false; break; }
       if (l == 10) STAMP(152);
-
+      if (ew) {
+        ld4h(sCc + c0, lw);
+        ld4h(sCc + C + c0, lb);
+        ld4h(sCc + 2 * C + c0, mu);
 #pragma unroll
-      for (int k = 0; k < CPL; ++k) {
-        const int c = tid + NT * k;
-        lw[k] = h2f(sCc[c]);
-        lb[k] = h2f(sCc[C + c]);
-        mu[k] = h2f(sCc[2 * C + c]);
-#pragma unroll
-        for (int b = 0; b < NB; ++b) prev[b][k] = h2f(sCc[(3 + b) * C + c]);
-      }
-      ln_regs<NB, CPL>(x, lw, lb, C, red);
-#pragma unroll
-      for (int b = 0; b < NB; ++b)
-#pragma unroll
-        for (int k = 0; k < CPL; ++k) {
-          const int c = tid + NT * k;
-          xk[(size_t)b * MLD + c] = f2h(x[b][k] + mu[k] * r16(prev[b][k] - x[b][k]));
-          if (cta == 0 && b < B) P.xln2[(size_t)b * C + c] = f2h(x[b][k]);
+        for (int b = 0; b < NB; ++b) {
+          ld4h(sCc + (3 + b) * C + c0, prev[b]);
+          st4h(sXr + (size_t)b * C + c0, x[b]);  // x1, the next layer's residual
         }
+      }
+      ln_regs<NB, E>(x, lw, lb, C, red);
+      if (ew) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          float m[E];
+#pragma unroll
+          for (int k = 0; k < E; ++k) m[k] = x[b][k] + mu[k] * r16(prev[b][k] - x[b][k]);
+          st4h(xk + (size_t)b * MLD + c0, m);
+          if (cta == 0 && b < B) st4h(P.xln2 + (size_t)b * C + c0, x[b]);
+        }
+      }
       __syncthreads();
       if (l == 10) STAMP(153);
       // key rows on the tensor cores: h = relu(fp16(x . Wk))^2 in fp16 (zero past f_nj)
@@ -887,8 +928,9 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
               ldsm_x4(vb + (uint32_t)(r * 64 + ((q ^ ((r >> 1) & 3)) << 4)), a);
               mma16816(d[u], a, hb0[ks], hb1[ks]);
             }
-          emit_tile<NB>(acc2, C, B, 16 * mt, 16, d[0], lane);
-          emit_tile<NB>(acc2, C, B, 16 * (mt + 8), 16, d[1], lane);
+          float* acc2r = acc2 + (size_t)(cta % NREP) * BC;
+          emit_tile<NB>(acc2r, C, B, 16 * mt, 16, d[0], lane);
+          emit_tile<NB>(acc2r, C, B, 16 * (mt + 8), 16, d[1], lane);
         }
       }
       if (l + 1 == P.L) {  // the value slice is consumed: head tile 2 takes its place
@@ -919,35 +961,33 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
   STAMP(250);
   {
     __half* xh = sXc;  // [NB][MLD]
-    const float* acc2 = P.acc + (size_t)(2 * P.L - 1) * BC;
+    const float* acc2 = P.acc + (size_t)(P.L - 1) * (1 + NREP) * BC + BC;
     __half* cmix_last = P.cmix_x + (size_t)(P.L - 1) * P.n_slots * C;
-    float lw[CPL], lb[CPL], x[NB][CPL];
-#pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      lw[k] = h2f(P.lnout_w[tid + NT * k]);
-      lb[k] = h2f(P.lnout_b[tid + NT * k]);
+    float lw[E] = {}, lb[E] = {}, x[NB][E];
+    if (ew) {
+      ld4h(P.lnout_w + c0, lw);
+      ld4h(P.lnout_b + c0, lb);
     }
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       const int bb = b < B ? b : 0;
+      if (ew) {
+        float xr[E], a[E];
+        ld_acc_rep(acc2 + (size_t)bb * C + c0, BC, a);
+        ld4h(sXr + (size_t)bb * C + c0, xr);
 #pragma unroll
-      for (int k = 0; k < CPL; ++k) {
-        const size_t o = (size_t)bb * C + tid + NT * k;
-        x[b][k] = r16(ldcg_h(P.x1 + o) + r16(__ldcg(acc2 + o)));
+        for (int k = 0; k < E; ++k) x[b][k] = r16(xr[k] + a[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < E; ++k) x[b][k] = 0.f;
       }
     }
-    if (cta == 0)
-      for (int b = 0; b < B; ++b)
+    if (cta == 0 && ew)
+      for (int b = 0; b < B; ++b) cp4h(cmix_last + (size_t)s_slot[b] * C + c0, P.xln2 + (size_t)b * C + c0);
+    ln_regs<NB, E>(x, lw, lb, C, red);
+    if (ew)
 #pragma unroll
-        for (int k = 0; k < CPL; ++k) {
-          const int c = tid + NT * k;
-          cmix_last[(size_t)s_slot[b] * C + c] = __ldcg(P.xln2 + (size_t)b * C + c);
-        }
-    ln_regs<NB, CPL>(x, lw, lb, C, red);
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-#pragma unroll
-      for (int k = 0; k < CPL; ++k) xh[(size_t)b * MLD + tid + NT * k] = f2h(x[b][k]);
+      for (int b = 0; b < NB; ++b) st4h(xh + (size_t)b * MLD + c0, x[b]);
     __syncthreads();
     const int ntile = (v1 - v0 + 31) / 32;
     for (int i = 0; i < ntile; ++i) {
@@ -1103,7 +1143,7 @@ int check_model_public(const rwkv7_model* m);
 // Workspace for the persistent path: activations + per-layer accumulators + the grid
 // barrier, laid out so one memset clears the accumulators and the barrier together.
 struct PersistWork {
-  __half *xres, *x1, *xln1, *xln2, *rkv, *ranks, *vfirst;
+  __half *xln1, *xln2, *rkv, *ranks, *vfirst;
   float* acc;
   GridBar* bar;
   size_t zero_bytes;
@@ -1118,15 +1158,13 @@ static size_t carve_persist(void* base, PersistWork* w, int L, int B, int C) {
   };
   const size_t BC = (size_t)B * C;
   PersistWork d;
-  d.xres = (__half*)take(BC * 2);
-  d.x1 = (__half*)take(BC * 2);
   d.xln1 = (__half*)take(BC * 2);
   d.xln2 = (__half*)take(BC * 2);
   d.rkv = (__half*)take(3 * BC * 2);
   d.ranks = (__half*)take((size_t)B * RWKV_RANK_SUM * 2);
   d.vfirst = (__half*)take(BC * 2);
   const size_t acc_off = off;
-  d.acc = (float*)take((size_t)L * 2 * BC * 4);
+  d.acc = (float*)take((size_t)L * (1 + NREP) * BC * 4);
   d.bar = (GridBar*)take(sizeof(GridBar));
   d.zero_bytes = off - acc_off;
   if (w) *w = d;
@@ -1188,7 +1226,7 @@ static int run_persist(const rwkv7_model* m, const int64_t* tokens, int B, const
   P.emb = (const __half*)m->emb; P.head = (const __half*)m->head;
   P.lnout_w = (const __half*)m->lnout_w; P.lnout_b = (const __half*)m->lnout_b;
   P.logits = (__half*)logits;
-  P.xres = w.xres; P.x1 = w.x1; P.xln1 = w.xln1; P.xln2 = w.xln2;
+  P.xln1 = w.xln1; P.xln2 = w.xln2;
   P.rkv = w.rkv; P.ranks = w.ranks; P.vfirst = w.vfirst; P.acc = w.acc; P.bar = w.bar;
   P.rnn = (float*)state->rnn;
   P.tmix_x = (__half*)state->tmix_x;
