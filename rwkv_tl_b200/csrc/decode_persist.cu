@@ -292,24 +292,14 @@ __device__ __forceinline__ void b_frag(const __half* x, int ld, int k0, int lane
     b0 = b1 = 0u;
   }
 }
-// acc[n][c0 + row] += D[row][n] of one 16 x 8 tile (rows < nvalid, whole quads), by
-// float4 atomics: row g's value of sequence n sits in lane 4 g + n / 2.
+// D[row][n] of one 16 x 8 tile into st[n * ld + r0 + row] (n < NB).
 template <int NB>
-__device__ __forceinline__ void emit_tile(float* acc, int C, int B, int c0, int nvalid,
-                                          const float (&d)[4], int lane) {
+__device__ __forceinline__ void stage_tile(float* st, int ld, int r0, const float (&d)[4], int lane) {
+  const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-  for (int n = 0; n < NB; ++n) {
-    const float lo = (n & 1) ? d[1] : d[0], hi = (n & 1) ? d[3] : d[2];
-    const float l1 = __shfl_down_sync(0xffffffffu, lo, 4), l2 = __shfl_down_sync(0xffffffffu, lo, 8),
-                l3 = __shfl_down_sync(0xffffffffu, lo, 12);
-    const float h1 = __shfl_down_sync(0xffffffffu, hi, 4), h2 = __shfl_down_sync(0xffffffffu, hi, 8),
-                h3 = __shfl_down_sync(0xffffffffu, hi, 12);
-    if (n < B && (lane & 15) == (n >> 1)) {
-      const int r = (lane >> 4) * 4;  // rows r .. r + 3 and r + 8 .. r + 11
-      if (r < nvalid) atomicAdd(reinterpret_cast<float4*>(acc + (size_t)n * C + c0 + r), make_float4(lo, l1, l2, l3));
-      if (r + 8 < nvalid)
-        atomicAdd(reinterpret_cast<float4*>(acc + (size_t)n * C + c0 + r + 8), make_float4(hi, h1, h2, h3));
-    }
+  for (int e = 0; e < 4; ++e) {
+    const int n = 2 * t + (e & 1);
+    if (n < NB) st[n * ld + r0 + g + (e >> 1) * 8] = d[e];
   }
 }
 // 32-row x C GEMV on the tensor cores: warp w takes rows 16 (w & 1) .. + 15 and
@@ -649,6 +639,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
       float* ybuf = vec + 7 * NB * 64;                        // [64]
       float* lora = ybuf + 64;                                // [4][NB][64]: v w a g 12
       __half* ygh = reinterpret_cast<__half*>(lora + 4 * NB * 64);  // [NB][72]
+      float* pst = reinterpret_cast<float*>(ygh + NB * 72);          // [NB][128] projection
       auto bvec = [&](int v) {
         return __half22float2(*reinterpret_cast<const __half2*>(sBc + v * 64 + 2 * lane));
       };
@@ -817,7 +808,14 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
           b_frag<NB>(ygh, 72, k0, lane, b0, b1);
           mma16816(d, a, b0, b1);
         }
-        emit_tile<NB>(acc1, C, B, b_c0 + r0, b_c1 - b_c0 - r0, d, lane);
+        stage_tile<NB>(pst, 128, r0, d, lane);
+        __syncthreads();
+        const int nq = (b_c1 - b_c0) / 4;  // whole quads of rows
+        for (int i = tid; i < B * nq; i += NT) {
+          const int n = i / nq, q = i % nq;
+          atomicAdd(reinterpret_cast<float4*>(acc1 + (size_t)n * C + b_c0 + 4 * q),
+                    *reinterpret_cast<const float4*>(pst + n * 128 + 4 * q));
+        }
       }
       if (jb == 0)  // new tmix state x (LN1 output) for this head's channels
         for (int i = tid; i < B * 64; i += NT) {
@@ -913,6 +911,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
          // takes the 16-row tiles w, w + 8, ...; the slice has a 64-byte swizzle (16-byte
          // chunk q of row c at q ^ ((c / 2) % 4))
         const uint32_t vb = saddr(sV);
+        float* vst = reinterpret_cast<float*>(sCc);  // [NB][C] staging (C vectors consumed)
         uint32_t hb0[2], hb1[2];
         b_frag<NB>(hh, HLD, 0, lane, hb0[0], hb1[0]);
         b_frag<NB>(hh, HLD, 16, lane, hb0[1], hb1[1]);
@@ -928,10 +927,13 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
               ldsm_x4(vb + (uint32_t)(r * 64 + ((q ^ ((r >> 1) & 3)) << 4)), a);
               mma16816(d[u], a, hb0[ks], hb1[ks]);
             }
-          float* acc2r = acc2 + (size_t)(cta % NREP) * BC;
-          emit_tile<NB>(acc2r, C, B, 16 * mt, 16, d[0], lane);
-          emit_tile<NB>(acc2r, C, B, 16 * (mt + 8), 16, d[1], lane);
+          stage_tile<NB>(vst, C, 16 * mt, d[0], lane);
+          stage_tile<NB>(vst, C, 16 * (mt + 8), d[1], lane);
         }
+        __syncthreads();
+        float* acc2r = acc2 + (size_t)(cta % NREP) * BC;
+        for (int i = tid; i < B * C / 4; i += NT)
+          atomicAdd(reinterpret_cast<float4*>(acc2r) + i, reinterpret_cast<const float4*>(vst)[i]);
       }
       if (l + 1 == P.L) {  // the value slice is consumed: head tile 2 takes its place
         __syncthreads();
