@@ -257,13 +257,16 @@ def run_b200(args, world, rank, local):
     # ---- roofline: the whole step, and its dominant kernel timed alone ----
     pk, pk_kind = peaks()
     wbytes = w.nbytes() - 2 * w.emb.numel()  # weights streamed per step (emb: rows only)
-    state_bytes = B * w.L * (w.H * 64 * 64 * 4 * 2 + 2 * w.C * 2 * 2)
-    io_bytes = B * (w.C * 2 + cfg.vocab * 2)
-    step_bytes = wbytes + state_bytes + io_bytes
+
+    def step_bytes_of(nb: int) -> int:  # weights once + per-sequence state r/w + io
+        return wbytes + nb * w.L * (w.H * 64 * 64 * 4 * 2 + 2 * w.C * 2 * 2) + \
+            nb * (w.C * 2 + cfg.vocab * 2)
+
+    step_bytes = step_bytes_of(B)
     kern = wkv_kernel_roofline(lib, B, w.H, dev, stream, pk["hbm_gbs"])
     extra = {}
     if rank == 0 and world == 1 and not args.quick:
-        extra = side_measurements(model, w, dev, stream)
+        extra = side_measurements(model, w, dev, stream, step_bytes_of, pk["hbm_gbs"])
 
     clocks = clk.summary()
     if rank == 0:
@@ -339,19 +342,25 @@ def wkv_kernel_roofline(lib, B: int, H: int, dev, stream, peak: float) -> dict:
             "avg_launch_us": ms * 1e3}
 
 
-def side_measurements(model, w, dev, stream) -> dict:
-    """Decode at B = 1, 8, 64 and prefill at T = 4096 (reported beside the headline)."""
+def side_measurements(model, w, dev, stream, step_bytes_of, hbm_gbs) -> dict:
+    """Decode at B = 1 .. 64 and prefill at T = 4096 (reported beside the headline); the
+    B = 1 step (the persistent single-kernel path) also against the HBM roofline."""
     from rwkv_tl_b200 import BatchedState, State
 
     out = {"decode_tokens_per_s_by_batch": {}}
-    for B in (1, 8, 64):
+    for B in (1, 2, 4, 8, 64):
         st = BatchedState(w.L, w.C, B, device=dev)
         tok = torch.randint(0, w.V, (B,), device=dev)
         f = lambda: model.decode_batch(tok, st)  # noqa: E731
         for _ in range(3):
             f()
-        ms = timed(f, 10, stream)
+        ms = timed(f, 50 if B <= 8 else 10, stream)
         out["decode_tokens_per_s_by_batch"][str(B)] = B / (ms * 1e-3)
+        if B == 1:
+            gbs = step_bytes_of(1) / (ms * 1e-3) / 1e9
+            out["decode_b1_roofline"] = {"bound": "hbm", "us_per_token": ms * 1e3,
+                                         "algorithmic_bytes_per_step": step_bytes_of(1),
+                                         "achieved": gbs, "unit": "GB/s", "frac": gbs / hbm_gbs}
     S = State(w.L, w.C, 64, device=dev)
     toks = torch.randint(0, w.V, (4096,), device=dev)
     f = lambda: model.prefill(toks, S)  # noqa: E731

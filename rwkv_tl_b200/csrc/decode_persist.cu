@@ -1,6 +1,7 @@
-// Small-batch decode (B <= 4 sequences, one token each) as ONE persistent kernel per
-// step: one CTA per SM, launched cooperatively so that every CTA is resident, with a
-// grid barrier between the three phases of each layer and before the head.
+// Small-batch decode (one token for each of B <= 2 sequences; B = 3, 4 as two launches)
+// as ONE persistent kernel per step: one CTA per SM, launched cooperatively so that
+// every CTA is resident, with a grid barrier between the three phases of each layer
+// and before the head.
 //
 // Reference: RWKV7Base.decode and its per-token kernels (demo/_rwkv7_base.py:74-87,
 // 153-206, 276-292; src/rwkv_tl/kernels/{lerp,gates,dplr}.py) with the decode rounding
@@ -101,6 +102,7 @@ struct PParams {
   int n_atask;        // phase-A tasks (CTAs past them idle in phase A)
   int gph, rows_b;    // CTAs per head in phase B, W_o rows per CTA
   int per_v;          // head rows per CTA
+  int slot_base;      // slot of sequence b when `slots` is null: slot_base + b
   const int64_t* tokens;
   const int* slots;
   const __half *emb, *head, *lnout_w, *lnout_b;
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
   for (int i = 0; i < MB_N; ++i) S.issued[i] = S.waited[i] = 0;
   if (tid < NB) {
     const int b = tid < B ? tid : 0;
-    s_slot[tid] = P.slots ? P.slots[b] : b;
+    s_slot[tid] = P.slots ? P.slots[b] : P.slot_base + b;
     s_tok[tid] = P.tokens[b];
   }
   if (tid == 0) {
@@ -1197,7 +1199,7 @@ bool decode_persist_supported(const rwkv7_model* m, int B, const rwkv7_state* st
   ATask tmp[MAXG];
   if (build_atasks(C, tmp, MAXG) > G) return false;
   if ((4 * C / 8 + G - 1) / G > FROWS / 8) return false;
-  const int NB = B == 1 ? 1 : (B == 2 ? 2 : 4);
+  const int NB = B == 1 ? 1 : 2;  // B = 3, 4 run as two launches of <= 2 sequences
   const size_t smem = smem_layout(NB, C, rows_b_of(C, G)).total;
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
@@ -1211,7 +1213,8 @@ size_t decode_persist_workspace(const rwkv7_model* m, int B) {
 
 template <int NB, int CPL>
 static int run_persist(const rwkv7_model* m, const int64_t* tokens, int B, const int* slots,
-                       const rwkv7_state* state, void* logits, void* ws, cudaStream_t st) {
+                       int slot_base, const rwkv7_state* state, void* logits, void* ws,
+                       cudaStream_t st) {
   const int L = m->n_layer, C = m->n_embd, H = C / RWKV_HD, G = device_sms();
   PersistWork w;
   carve_persist(ws, &w, L, B, C);
@@ -1224,7 +1227,7 @@ static int run_persist(const rwkv7_model* m, const int64_t* tokens, int B, const
   P.gph = G / H;
   P.rows_b = rows_b_of(C, G);
   P.per_v = (m->vocab + G - 1) / G;
-  P.tokens = tokens; P.slots = slots;
+  P.tokens = tokens; P.slots = slots; P.slot_base = slot_base;
   P.emb = (const __half*)m->emb; P.head = (const __half*)m->head;
   P.lnout_w = (const __half*)m->lnout_w; P.lnout_b = (const __half*)m->lnout_b;
   P.logits = (__half*)logits;
@@ -1283,15 +1286,24 @@ static int run_persist(const rwkv7_model* m, const int64_t* tokens, int B, const
   return rwkv_check_launch("decode_persist");
 }
 
+// B <= 2 in one launch; B = 3, 4 as two launches of <= 2 sequences (the two-sequence
+// layout is the largest that fits shared memory, and two of its steps beat one step of
+// the three-kernel path).
 int decode_persist_run(const rwkv7_model* m, const int64_t* tokens, int B, const int* slots,
                        const rwkv7_state* state, void* logits, void* ws, cudaStream_t st) {
   const bool c768 = m->n_embd == 768;
-  if (B == 1) return c768 ? run_persist<1, 3>(m, tokens, B, slots, state, logits, ws, st)
-                          : run_persist<1, 4>(m, tokens, B, slots, state, logits, ws, st);
-  if (B == 2) return c768 ? run_persist<2, 3>(m, tokens, B, slots, state, logits, ws, st)
-                          : run_persist<2, 4>(m, tokens, B, slots, state, logits, ws, st);
-  return c768 ? run_persist<4, 3>(m, tokens, B, slots, state, logits, ws, st)
-              : run_persist<4, 4>(m, tokens, B, slots, state, logits, ws, st);
+  auto one = [&](int off, int nb) {
+    const int64_t* t = tokens + off;
+    const int* sl = slots ? slots + off : nullptr;
+    void* lg = static_cast<__half*>(logits) + (size_t)off * m->vocab;
+    if (nb == 1) return c768 ? run_persist<1, 3>(m, t, 1, sl, off, state, lg, ws, st)
+                             : run_persist<1, 4>(m, t, 1, sl, off, state, lg, ws, st);
+    return c768 ? run_persist<2, 3>(m, t, nb, sl, off, state, lg, ws, st)
+                : run_persist<2, 4>(m, t, nb, sl, off, state, lg, ws, st);
+  };
+  if (B <= 2) return one(0, B);
+  const int rc = one(0, 2);
+  return rc ? rc : one(2, B - 2);
 }
 
 #if PERSIST_STAMPS
