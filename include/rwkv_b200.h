@@ -201,10 +201,14 @@ int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* batch,
                   void* stream);
 
 /* One decode step of n_seqs (1..8) sequences, one token each, through the
- * small-batch path: three fused kernels per layer (LN+mix+r/k/v/LoRA-down GEMV;
- * per-head gates+wkv+GroupNorm+output projection; LN2+FFN) and the head GEMV,
- * chained with programmatic dependent launch so each kernel's weights stream
- * into L2 while the previous kernel finishes. Decode rounding semantics.
+ * small-batch path. n_seqs <= 4 (two sequences per launch): one persistent
+ * cooperative kernel per launch, one CTA per SM, grid barriers between the
+ * three phases of each layer, weight slices staged into shared memory by TMA
+ * one phase ahead, GEMVs on the tensor cores. n_seqs 5..8 (or when the device
+ * or pointer alignment does not allow the persistent kernel): three fused
+ * kernels per layer (LN+mix+r/k/v/LoRA-down GEMV; per-head gates+wkv+GroupNorm+
+ * output projection; LN2+FFN) and the head GEMV, chained with programmatic
+ * dependent launch. Decode rounding semantics.
  * tokens: device int64 [n_seqs]; slots: device int [n_seqs] or NULL; logits:
  * fp16 [n_seqs, V]. n_embd must be 768 or 1024. Same result as
  * rwkv7_forward with RWKV_SEM_DECODE on one token per sequence. */
