@@ -367,7 +367,47 @@ def side_measurements(model, w, dev, stream, step_bytes_of, hbm_gbs) -> dict:
     f()
     ms = timed(f, 3, stream)
     out["prefill_T4096"] = {"tokens_per_s": 4096 / (ms * 1e-3), "ms": ms}
+    out["continuous_batching"] = continuous_batching(model, w, dev, stream, n_seqs=256,
+                                                     max_new=128, max_batch=256)
     return out
+
+
+def continuous_batching(model, w, dev, stream, n_seqs: int, max_new: int, max_batch: int,
+                        world: int = 1, rank: int = 0, seed: int = 4) -> dict:
+    """Config 4: n_seqs requests, prompt lengths ~U[16, 2048] and token ids uniform
+    (seeded), max_new greedy tokens each, through ``ContinuousBatcher`` with decode
+    batches of up to max_batch; sequences sharded over ranks by prompt length. Timed
+    with CUDA events around the whole run (the host scheduler included)."""
+    from rwkv_tl_b200 import ContinuousBatcher, Request
+    from rwkv_tl_b200.shard import shard_by_length
+
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(16, 2049, (n_seqs,), generator=g).tolist()
+    prompts = [torch.randint(0, w.V, (n,), generator=g) for n in lens]
+    mine = shard_by_length(lens, world)[rank]
+    eng = model.model if hasattr(model, "model") else model
+    warm = ContinuousBatcher(eng, max_batch=max_batch, prefill_tokens=4096)
+    for i in mine[:8]:
+        warm.submit(Request(i, prompts[i][:64], 4))
+    warm.run()
+    del warm
+    b = ContinuousBatcher(eng, max_batch=max_batch, prefill_tokens=4096)
+    for i in mine:
+        b.submit(Request(i, prompts[i], max_new))
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    b.run()
+    e.record(stream)
+    torch.cuda.synchronize()
+    sec = max_over_ranks(s.elapsed_time(e) * 1e-3, world)
+    prompt_tok = sum(lens) if world > 1 else sum(lens[i] for i in mine)
+    gen_tok = (n_seqs if world > 1 else len(mine)) * max_new
+    return {"workload": f"{n_seqs} requests, prompts U[16,2048], {max_new} greedy tokens each, "
+                        f"decode batch <= {max_batch} per GPU", "seconds": sec,
+            "tokens_per_s": (prompt_tok + gen_tok) / sec, "generated_tokens_per_s": gen_tok / sec,
+            "prompt_tokens": prompt_tok, "generated_tokens": gen_tok, "scheduler_steps": b.steps}
 
 
 def run_profile(args):
@@ -395,6 +435,24 @@ def run_profile(args):
     print(f"{args.profile}: {ms:.3f} ms per call", flush=True)
 
 
+def run_continuous(args, world, rank, local):
+    from rwkv_tl_b200 import RWKV7Weight, make_rwkv7
+    from rwkv_tl_b200.synth import CONFIG_0_4B, synth_checkpoint
+
+    dev = torch.device("cuda", local)
+    w = RWKV7Weight(synth_checkpoint(CONFIG_0_4B, seed=0, device=dev), device=dev)
+    model = make_rwkv7(dev, backend="b200", use_graph=False)(w)
+    stream = torch.cuda.current_stream(dev)
+    with Clocks(local) as clk:
+        r = continuous_batching(model, w, dev, stream, n_seqs=args.continuous, max_new=128,
+                                max_batch=args.batch, world=world, rank=rank)
+    if rank == 0:
+        print(json.dumps({"metric": "continuous batching tokens/s (prompt + generated), config 4",
+                          "value": r["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+                          "higher_is_better": True, "scaling": "strong", "dtype": "f16",
+                          "data": "synthetic", "config": r, "clocks": clk.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -408,12 +466,17 @@ def main():
                     help="profiling driver: run only K decode steps (--batch) or K prefills "
                          "(--seq-len) and print the per-call time, no JSON line")
     ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--continuous", type=int, default=0, metavar="N_SEQS",
+                    help="run only config 4 (continuous batching of N_SEQS requests, 128 new "
+                         "tokens each, sharded over the ranks) and print its JSON line")
     args = ap.parse_args()
     world, rank, local = dist_setup() if args.impl == "b200" or int(
         os.environ.get("WORLD_SIZE", "1")) == 1 else (int(os.environ["WORLD_SIZE"]),
                                                       int(os.environ.get("RANK", "0")), 0)
     if args.profile:
         run_profile(args)
+    elif args.continuous and args.impl == "b200":
+        run_continuous(args, world, rank, local)
     elif args.impl == "reference":
         run_reference(args, world, rank)
     else:

@@ -9,10 +9,11 @@ from .cuda_graph import CUDAGraph, make_graph_cls
 from .factory import make_rwkv7
 from .model import RWKV7B200, RWKV7Model
 from .sampling import sample_logits
+from .serve import ContinuousBatcher, Request
 from .state import BatchedState, State
 from .weight import RWKV7Weight
 
 __all__ = [
-    "BatchedState", "CUDAGraph", "RWKV7B200", "RWKV7Model", "RWKV7Weight", "State",
-    "make_graph_cls", "make_rwkv7", "sample_logits",
+    "BatchedState", "ContinuousBatcher", "CUDAGraph", "RWKV7B200", "RWKV7Model", "RWKV7Weight",
+    "Request", "State", "make_graph_cls", "make_rwkv7", "sample_logits",
 ]
