@@ -126,9 +126,10 @@ int rwkv_b200_abi_version(void);
  * captured CUDA graph replays its kernels without passing through here). */
 unsigned long long rwkv_b200_launch_count(void);
 /* Nonzero if, since the last call, a kernel on the current device gave up on a
- * bounded wait instead of spinning forever: bit 0 a GEMM pipeline barrier, bit 1 a
- * grid barrier of the persistent decode kernel. Reading clears it. Synchronous
- * (reads device memory). */
+ * bounded wait instead of spinning forever (bit 0 a GEMM pipeline barrier, bit 1 a
+ * grid barrier of the persistent decode kernel), or a chunked-wkv kernel found a
+ * sequence table out of range and skipped that sequence (bit 2). Reading clears it.
+ * Synchronous (reads device memory). */
 int rwkv_b200_device_error(void);
 
 /* wkv7 DPLR step, batched over n_seq independent sequences (T = 1):

@@ -36,10 +36,29 @@ int rwkv_check_launch(const char* what) {
 extern "C" const char* rwkv_b200_last_error(void) { return g_err; }
 extern "C" int rwkv_b200_abi_version(void) { return RWKV_B200_ABI_VERSION; }
 int gemm_tc_timeout_flag();
+bool rwkv_pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("RWKV_B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+namespace {
+thread_local bool t_chain_first = true;
+}
+void rwkv_chain_begin() { t_chain_first = true; }
+bool rwkv_chain_take_pdl() {
+  const bool first = t_chain_first;
+  t_chain_first = false;
+  return !first && rwkv_pdl_enabled();
+}
+
 int decode_persist_timeout_flag();
+int wkv_chunk_bad_flag();
 extern "C" int rwkv_b200_device_error(void) {
-  const int a = gemm_tc_timeout_flag(), b = decode_persist_timeout_flag();
-  return a | (b << 1);
+  const int a = gemm_tc_timeout_flag(), b = decode_persist_timeout_flag(), c = wkv_chunk_bad_flag();
+  return a | (b << 1) | (c << 2);
 }
 
 extern "C" unsigned long long rwkv_b200_launch_count(void) {
@@ -71,7 +90,7 @@ size_t wkv_chunk_record_bytes(int M, int S, int H);
 int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
                        const __half* a, const __half* b, float* rnn, const int* cu,
                        const int* slots, __half* ybuf, float* rec, int* chunk_cu, int M, int S,
-                       int H, cudaStream_t st);
+                       int H, int n_slots, cudaStream_t st);
 int launch_wkv_epilogue(int sem, const __half* ybuf, const __half* rbuf, const __half* gbuf,
                         size_t plane, const __half* r_k, const __half* lnx_w,
                         const __half* lnx_b, __half* yg, int M, int C, cudaStream_t st);
@@ -216,6 +235,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const int ns = state->n_slots;
   const __half* emb = (const __half*)model->emb;
   const bool chunked = use_chunked_wkv(M, S);
+  rwkv_chain_begin();
   // columns 32..63 of the rank buffer (the zero padding of rank v) must read as zero
   if (cudaMemsetAsync(w.ranks, 0, (size_t)M * RANKS_LD * sizeof(__half), st) != cudaSuccess)
     return rwkv_check_launch("ranks memset");
@@ -276,7 +296,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
       // gbuf planes: 0 w, 1 k, 2 v, 3 A (k_hat), 4 B; r from the rkv buffer
       TRY(launch_wkv_chunked(w.rkv, w.gbuf, w.gbuf + MC, w.gbuf + 2 * MC, w.gbuf + 3 * MC,
                              w.gbuf + 4 * MC, st_rnn, b->cu_seqlens, b->slots, w.xk, w.chunk_rec,
-                             w.chunk_cu, M, S, H, st));
+                             w.chunk_cu, M, S, H, ns, st));
       TRY(launch_wkv_epilogue(sem, w.xk, w.rkv, w.gbuf, MC, (const __half*)Lw.r_k,
                               (const __half*)Lw.lnx_w, (const __half*)Lw.lnx_b, w.yg, M, C, st));
     } else

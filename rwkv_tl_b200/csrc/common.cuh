@@ -106,3 +106,50 @@ __device__ __forceinline__ void block_sum(float (&v)[NV], float* red) {
 // Host side: record an error message for rwkv_b200_last_error().
 void rwkv_set_error(const char* fmt, ...);
 int rwkv_check_launch(const char* what);
+
+// Programmatic dependent launch. Kernels of a library call after its first are
+// launched with programmatic stream serialization. Every such kernel calls
+// grid_dep_wait() before its first access to memory written by an earlier kernel
+// (it returns once the preceding grid has completed and its writes are visible) and
+// only then grid_dep_trigger(), which lets the next kernel launch and run its
+// prologue (barrier and TMEM set-up, the GEMM's first weight tiles) while this one
+// works. Triggering after the wait keeps the chain one kernel deep: a kernel is never
+// launched before its predecessor's predecessor has completed, so data written two
+// or more kernels back is complete and visible to it.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#define RWKV_GRID_DEP_ENTRY() \
+  do {                        \
+    grid_dep_wait();          \
+    grid_dep_trigger();       \
+  } while (0)
+
+bool rwkv_pdl_enabled();  // RWKV_B200_PDL=0 turns the attribute off (plain stream order)
+// Start of a library call: its first launch depends on whatever the caller queued
+// before (copies, memsets, other libraries' kernels) in plain stream order; only
+// launches after it, within the call, get the programmatic edge.
+void rwkv_chain_begin();
+bool rwkv_chain_take_pdl();  // attribute for this launch? (false once per chain begin)
+
+template <typename... KArgs, typename... Args>
+int rwkv_launch(const char* name, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = rwkv_chain_take_pdl() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+  if (e != cudaSuccess) {
+    rwkv_set_error("%s: launch failed: %s", name, cudaGetErrorString(e));
+    return RWKV_ERR_CUDA;
+  }
+  return rwkv_check_launch(name);
+}

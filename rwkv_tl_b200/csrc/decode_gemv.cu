@@ -608,8 +608,10 @@ __global__ void __launch_bounds__(NT) k_dec_head(const __half* __restrict__ head
 }
 
 // ---------------------------------------------------------------------------
+// `pdl` false: plain stream order (the first launch of a step follows the memset and
+// whatever the caller queued before it).
 template <typename K, typename... Args>
-int launch_pdl(K kernel, dim3 grid, size_t smem, cudaStream_t st, const char* name,
+int launch_pdl(bool pdl, K kernel, dim3 grid, size_t smem, cudaStream_t st, const char* name,
                Args... args) {
   // dynamic + static shared memory may exceed the default 48 KiB: always opt in
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -626,7 +628,7 @@ int launch_pdl(K kernel, dim3 grid, size_t smem, cudaStream_t st, const char* na
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   e = cudaLaunchKernelEx(&cfg, kernel, args...);
   if (e != cudaSuccess) {
     rwkv_set_error("%s: launch failed: %s", name, cudaGetErrorString(e));
@@ -700,15 +702,15 @@ int run_decode(const rwkv7_model* m, const int64_t* tokens, int B, const int* sl
     P.tmix_x = (__half*)state->tmix_x + (size_t)l * ns * C;
     P.cmix_x = (__half*)state->cmix_x + (size_t)l * ns * C;
     P.cmix_x_prev = l ? (__half*)state->cmix_x + (size_t)(l - 1) * ns * C : nullptr;
-    if ((rc = launch_pdl(k_dec_a<NB, CPL>, dim3(148), smem_a, st, "decode_gemv A", D, P)))
+    if ((rc = launch_pdl(l > 0, k_dec_a<NB, CPL>, dim3(148), smem_a, st, "decode_gemv A", D, P)))
       return rc;
-    if ((rc = launch_pdl(k_dec_b<NB>, dim3(H), smem_b, st, "decode_gemv B", D, P))) return rc;
-    if ((rc = launch_pdl(k_dec_c<NB, CPL>, dim3(4 * C / 32), smem_c, st, "decode_gemv C", D, P)))
+    if ((rc = launch_pdl(true, k_dec_b<NB>, dim3(H), smem_b, st, "decode_gemv B", D, P))) return rc;
+    if ((rc = launch_pdl(true, k_dec_c<NB, CPL>, dim3(4 * C / 32), smem_c, st, "decode_gemv C", D, P)))
       return rc;
   }
   P.acc2 = w.acc + (size_t)(2 * L - 1) * BC;
   P.cmix_x = (__half*)state->cmix_x + (size_t)(L - 1) * ns * C;
-  return launch_pdl(k_dec_head<NB, CPL>, dim3(296), (size_t)NB * C * 2, st, "decode_gemv head",
+  return launch_pdl(true, k_dec_head<NB, CPL>, dim3(296), (size_t)NB * C * 2, st, "decode_gemv head",
                     (const __half*)m->head, (const __half*)m->lnout_w, (const __half*)m->lnout_b,
                     P, m->vocab, (__half*)logits);
 }

@@ -38,6 +38,7 @@ __global__ void __launch_bounds__(256) k_gates_ew(
     __half* __restrict__ vfirst,        // [M, C] written on layer 0, read otherwise
     __half* __restrict__ gout,          // 6 x [M, C]: w, k, v, A, B, g
     int M, int C, int H, int layer0) {
+  RWKV_GRID_DEP_ENTRY();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int m = blockIdx.x, h = blockIdx.y * 8 + warp;
   if (h >= H) return;
@@ -121,11 +122,8 @@ int launch_gates_ew(int sem, const void* lora, const __half* rkv, const __half* 
   const int H = C / RWKV_HD;
   dim3 grid(M, (H + 7) / 8);
   if (sem == SEM_DECODE)
-    k_gates_ew<SEM_DECODE, float><<<grid, 256, 0, st>>>((const float*)lora, rkv, w0, a0, v0, k_k,
-                                                        k_a, vfirst, gout, M, C, H, layer0);
-  else
-    k_gates_ew<SEM_PREFILL, __half><<<grid, 256, 0, st>>>((const __half*)lora, rkv, w0, a0, v0,
-                                                          k_k, k_a, vfirst, gout, M, C, H,
-                                                          layer0);
-  return rwkv_check_launch("gates_ew");
+    return rwkv_launch("gates_ew", k_gates_ew<SEM_DECODE, float>, grid, dim3(256), 0, st,
+                       (const float*)lora, rkv, w0, a0, v0, k_k, k_a, vfirst, gout, M, C, H, layer0);
+  return rwkv_launch("gates_ew", k_gates_ew<SEM_PREFILL, __half>, grid, dim3(256), 0, st,
+                     (const __half*)lora, rkv, w0, a0, v0, k_k, k_a, vfirst, gout, M, C, H, layer0);
 }

@@ -54,6 +54,7 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 
 template <int EPI>
 __global__ void __launch_bounds__(NTHREADS) k_gemm_mma(const GemmGroup grp) {
+  RWKV_GRID_DEP_ENTRY();
   extern __shared__ __align__(128) __half smem[];
   if ((int)blockIdx.z >= grp.n) return;
   const rwkv7_gemm_problem& P = grp.p[blockIdx.z];
@@ -167,8 +168,7 @@ int launch_group(const GemmGroup& g, cudaStream_t st) {
     gy = max(gy, (g.p[i].M + BM - 1) / BM);
   }
   if (gx == 0 || gy == 0) return RWKV_OK;
-  k_gemm_mma<EPI><<<dim3(gx, gy, g.n), NTHREADS, smem, st>>>(g);
-  return rwkv_check_launch("gemm_mma");
+  return rwkv_launch("gemm_mma", k_gemm_mma<EPI>, dim3(gx, gy, g.n), dim3(NTHREADS), smem, st, g);
 }
 
 }  // namespace
@@ -231,6 +231,7 @@ int gemm_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStream_t
 
 extern "C" int rwkv7_gemm_f16(const rwkv7_gemm_problem* problems, int n_problems, int epilogue,
                               void* stream) {
+  rwkv_chain_begin();
   int rc = gemm_validate(problems, n_problems);
   if (rc) return rc;
   for (int i = 0; i < n_problems; ++i)

@@ -171,13 +171,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
   const int split = blockIdx.z / prm.n_problems;
   const TcProblem& P = prm.p[g];
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-  if (n0 >= P.N || m0 >= P.M) return;
+  if (n0 >= P.N || m0 >= P.M) {
+    grid_dep_wait();
+    return;
+  }
   const int KB = P.K / BK;
   const int kb_per = (KB + prm.splits - 1) / prm.splits;
   const int kb0 = split * kb_per, kb1 = min(KB, kb0 + kb_per);
   // a K-slice past the end still writes its (zero) partial tile for the reduce
   const bool no_k = kb0 >= kb1;
-  if (no_k && prm.splits == 1) return;
+  if (no_k && prm.splits == 1) {
+    grid_dep_wait();
+    return;
+  }
 
   // shared memory: [A stages][B stages] (1024-aligned) | barriers | tmem address
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -213,8 +219,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      int issued = 0;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      // B (weights, never written by the preceding kernels) of the first stages goes
+      // out before the programmatic wait; A (activations) only after it
+      const int pre = min(STAGES, kb1 - kb0);
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full[i], A_BYTES + B_BYTES);
+        tma_load_2d(sB + i * B_BYTES, &prm.tb[g], &full[i], (kb0 + i) * BK, n0);
+      }
+      grid_dep_wait();
+      grid_dep_trigger();
+      for (int i = 0; i < pre; ++i) tma_load_2d(sA + i * A_BYTES, &prm.ta[g], &full[i], (kb0 + i) * BK, m0);
+      int issued = pre;
+      for (int kb = kb0 + pre; kb < kb1; ++kb) {
         const int s = issued % STAGES;
         const uint32_t round = issued / STAGES;
         if (!mbar_wait(&empty[s], (round & 1) ^ 1)) break;
@@ -226,8 +242,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
       // drain: never leave the CTA while copies may still land in shared memory
       for (int i = max(0, issued - STAGES); i < issued; ++i)
         mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+    } else {
+      grid_dep_wait();
+      grid_dep_trigger();
     }
   } else if (warp == 1) {
+    grid_dep_wait();
+    grid_dep_trigger();
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t idesc = instr_desc<BN>();
@@ -254,6 +275,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    grid_dep_wait();
+    grid_dep_trigger();
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const bool ok = mbar_wait(tmem_full, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -315,6 +338,7 @@ struct ReduceParams {
 // Split-K reduce: C = epi(sum_s ws[s]) for every problem. grid = (ceil(max M*N/4 / 256), n).
 template <int EPI>
 __global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ ReduceParams rp) {
+  RWKV_GRID_DEP_ENTRY();
   const TcProblem& P = rp.p[blockIdx.y];
   const size_t MN = (size_t)P.M * P.N;
   const size_t i = ((size_t)blockIdx.x * 256 + threadIdx.x) * 4;
@@ -423,8 +447,8 @@ int launch_tc(const TcParams& prm, dim3 grid, cudaStream_t st) {
     }
     done[dev] = true;
   }
-  k_gemm_tc<BN, EPI, STAGES><<<grid, NTHREADS, smem_bytes<BN, STAGES>(), st>>>(prm);
-  return rwkv_check_launch("gemm_tc");
+  return rwkv_launch("gemm_tc", k_gemm_tc<BN, EPI, STAGES>, grid, dim3(NTHREADS),
+                     (size_t)smem_bytes<BN, STAGES>(), st, prm);
 }
 
 }  // namespace
@@ -517,15 +541,13 @@ int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, 
     max_mn = max(max_mn, (size_t)p[i].M * p[i].N);
   }
   dim3 rgrid((unsigned)((max_mn / 4 + 255) / 256), n);
-  switch (epi) {
-    case RWKV_EPI_STORE: k_splitk_reduce<RWKV_EPI_STORE><<<rgrid, 256, 0, st>>>(rp); break;
-    case RWKV_EPI_RESID: k_splitk_reduce<RWKV_EPI_RESID><<<rgrid, 256, 0, st>>>(rp); break;
-    case RWKV_EPI_RELUSQ: k_splitk_reduce<RWKV_EPI_RELUSQ><<<rgrid, 256, 0, st>>>(rp); break;
-    case RWKV_EPI_STORE_F32: k_splitk_reduce<RWKV_EPI_STORE_F32><<<rgrid, 256, 0, st>>>(rp); break;
-    case RWKV_EPI_LORA_ACT: k_splitk_reduce<RWKV_EPI_LORA_ACT><<<rgrid, 256, 0, st>>>(rp); break;
-    default: k_splitk_reduce<RWKV_EPI_LORA_ACT2><<<rgrid, 256, 0, st>>>(rp); break;
-  }
-  return rwkv_check_launch("splitk_reduce");
+  auto red = epi == RWKV_EPI_STORE     ? k_splitk_reduce<RWKV_EPI_STORE>
+             : epi == RWKV_EPI_RESID     ? k_splitk_reduce<RWKV_EPI_RESID>
+             : epi == RWKV_EPI_RELUSQ    ? k_splitk_reduce<RWKV_EPI_RELUSQ>
+             : epi == RWKV_EPI_STORE_F32 ? k_splitk_reduce<RWKV_EPI_STORE_F32>
+             : epi == RWKV_EPI_LORA_ACT  ? k_splitk_reduce<RWKV_EPI_LORA_ACT>
+                                         : k_splitk_reduce<RWKV_EPI_LORA_ACT2>;
+  return rwkv_launch("splitk_reduce", red, rgrid, dim3(256), 0, st, rp);
 }
 
 // Host read of the device timeout flag (cleared on read); nonzero means a bounded wait gave up.

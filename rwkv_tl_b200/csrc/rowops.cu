@@ -64,6 +64,7 @@ __global__ void k_tmix_rows(__half* __restrict__ x, const int64_t* __restrict__ 
                             const __half* __restrict__ state_x, const int* __restrict__ row_seq,
                             const int* __restrict__ cu, const int* __restrict__ slots,
                             __half* __restrict__ xmix, __half* __restrict__ xlast, int M, int C) {
+  RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32 * 2];
   const int m = blockIdx.x, c = threadIdx.x * 4;
   const int s = row_seq[m];
@@ -94,6 +95,7 @@ __global__ void k_cmix_rows(const __half* __restrict__ x, const __half* __restri
                             const __half* __restrict__ state_x, const int* __restrict__ row_seq,
                             const int* __restrict__ cu, const int* __restrict__ slots,
                             __half* __restrict__ xk, __half* __restrict__ xlast, int C) {
+  RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32 * 2];
   const int m = blockIdx.x, c = threadIdx.x * 4;
   const int s = row_seq[m];
@@ -112,6 +114,7 @@ __global__ void k_cmix_rows(const __half* __restrict__ x, const __half* __restri
 __global__ void k_ln_rows(const __half* __restrict__ x, const int* __restrict__ rows,
                           const __half* __restrict__ w, const __half* __restrict__ b,
                           __half* __restrict__ out, int C) {
+  RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32];
   const int i = blockIdx.x, c = threadIdx.x * 4;
   float4 v[1];
@@ -125,6 +128,7 @@ __global__ void k_ln_rows(const __half* __restrict__ x, const int* __restrict__ 
 __global__ void k_scatter_state_x(const __half* __restrict__ xlast, __half* __restrict__ tmix_x,
                                   __half* __restrict__ cmix_x, const int* __restrict__ slots,
                                   int S, int n_slots, int C) {
+  RWKV_GRID_DEP_ENTRY();
   const int s = blockIdx.x, l = blockIdx.y, which = blockIdx.z, c = threadIdx.x * 4;
   const int slot = slots ? slots[s] : s;
   const __half* src = xlast + (((size_t)l * 2 + which) * S + s) * C + c;
@@ -136,36 +140,27 @@ int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* em
                      const __half* ln_w, const __half* ln_b, const __half* mix6,
                      const __half* state_x, const int* row_seq, const int* cu, const int* slots,
                      __half* xmix, __half* xlast, int M, int C, cudaStream_t st) {
-  if (sem == SEM_DECODE)
-    k_tmix_rows<SEM_DECODE><<<M, C / 4, 0, st>>>(x, tokens, emb, ln_w, ln_b, mix6, state_x, row_seq,
-                                                 cu, slots, xmix, xlast, M, C);
-  else
-    k_tmix_rows<SEM_PREFILL><<<M, C / 4, 0, st>>>(x, tokens, emb, ln_w, ln_b, mix6, state_x,
-                                                  row_seq, cu, slots, xmix, xlast, M, C);
-  return rwkv_check_launch("tmix_rows");
+  return rwkv_launch("tmix_rows", sem == SEM_DECODE ? k_tmix_rows<SEM_DECODE> : k_tmix_rows<SEM_PREFILL>,
+                     dim3(M), dim3(C / 4), 0, st, x, tokens, emb, ln_w, ln_b, mix6, state_x, row_seq,
+                     cu, slots, xmix, xlast, M, C);
 }
 
 int launch_cmix_rows(int sem, const __half* x, const __half* ln_w, const __half* ln_b,
                      const __half* mu, const __half* state_x, const int* row_seq, const int* cu,
                      const int* slots, __half* xk, __half* xlast, int M, int C, cudaStream_t st) {
-  if (sem == SEM_DECODE)
-    k_cmix_rows<SEM_DECODE><<<M, C / 4, 0, st>>>(x, ln_w, ln_b, mu, state_x, row_seq, cu, slots, xk,
-                                                 xlast, C);
-  else
-    k_cmix_rows<SEM_PREFILL><<<M, C / 4, 0, st>>>(x, ln_w, ln_b, mu, state_x, row_seq, cu, slots,
-                                                  xk, xlast, C);
-  return rwkv_check_launch("cmix_rows");
+  return rwkv_launch("cmix_rows", sem == SEM_DECODE ? k_cmix_rows<SEM_DECODE> : k_cmix_rows<SEM_PREFILL>,
+                     dim3(M), dim3(C / 4), 0, st, x, ln_w, ln_b, mu, state_x, row_seq, cu, slots, xk,
+                     xlast, C);
 }
 
 int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __half* b,
                    __half* out, int n, int C, cudaStream_t st) {
   if (n == 0) return RWKV_OK;
-  k_ln_rows<<<n, C / 4, 0, st>>>(x, rows, w, b, out, C);
-  return rwkv_check_launch("ln_rows");
+  return rwkv_launch("ln_rows", k_ln_rows, dim3(n), dim3(C / 4), 0, st, x, rows, w, b, out, C);
 }
 
 int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,
                            int S, int L, int n_slots, int C, cudaStream_t st) {
-  k_scatter_state_x<<<dim3(S, L, 2), C / 4, 0, st>>>(xlast, tmix_x, cmix_x, slots, S, n_slots, C);
-  return rwkv_check_launch("scatter_state_x");
+  return rwkv_launch("scatter_state_x", k_scatter_state_x, dim3(S, L, 2), dim3(C / 4), 0, st, xlast,
+                     tmix_x, cmix_x, slots, S, n_slots, C);
 }

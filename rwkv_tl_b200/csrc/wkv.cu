@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(256) k_wkv_tokens(
     const __half* __restrict__ r_k, const __half* __restrict__ lnx_w,
     const __half* __restrict__ lnx_b, float* __restrict__ rnn, const int* __restrict__ cu,
     const int* __restrict__ slots, __half* __restrict__ yg, int C) {
+  RWKV_GRID_DEP_ENTRY();
   __shared__ float ybuf[2][RWKV_HD];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int seq = blockIdx.x, h = blockIdx.y, H = gridDim.y;
@@ -258,6 +259,7 @@ __global__ void __launch_bounds__(256, 5) k_wkv_decode(
     const DecVecs X, const __half* __restrict__ r_k, const __half* __restrict__ lnx_w,
     const __half* __restrict__ lnx_b, float* __restrict__ rnn, const int* __restrict__ slots,
     __half* __restrict__ yg, int C) {
+  RWKV_GRID_DEP_ENTRY();
   __shared__ float ybuf[RWKV_HD];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int m = blockIdx.x, h = blockIdx.y, H = gridDim.y;
@@ -310,19 +312,11 @@ int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t pl
   if (n_seqs * C == (int)plane) {  // one token per sequence
     const DecVecs X = {rbuf, gbuf, gbuf + plane, gbuf + 2 * plane, gbuf + 3 * plane,
                        gbuf + 4 * plane, gbuf + 5 * plane};
-    if (sem == SEM_DECODE)
-      k_wkv_decode<SEM_DECODE><<<grid, 256, 0, st>>>(X, r_k, lnx_w, lnx_b, rnn, slots, yg, C);
-    else
-      k_wkv_decode<SEM_PREFILL><<<grid, 256, 0, st>>>(X, r_k, lnx_w, lnx_b, rnn, slots, yg, C);
-    return rwkv_check_launch("wkv_decode");
+    return rwkv_launch("wkv_decode", sem == SEM_DECODE ? k_wkv_decode<SEM_DECODE> : k_wkv_decode<SEM_PREFILL>,
+                       grid, dim3(256), 0, st, X, r_k, lnx_w, lnx_b, rnn, slots, yg, C);
   }
-  if (sem == SEM_DECODE)
-    k_wkv_tokens<SEM_DECODE><<<grid, 256, 0, st>>>(rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn, cu,
-                                                   slots, yg, C);
-  else
-    k_wkv_tokens<SEM_PREFILL><<<grid, 256, 0, st>>>(rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn, cu,
-                                                    slots, yg, C);
-  return rwkv_check_launch("wkv_tokens");
+  return rwkv_launch("wkv_tokens", sem == SEM_DECODE ? k_wkv_tokens<SEM_DECODE> : k_wkv_tokens<SEM_PREFILL>,
+                     grid, dim3(256), 0, st, rbuf, gbuf, plane, r_k, lnx_w, lnx_b, rnn, cu, slots, yg, C);
 }
 
 extern "C" int rwkv7_dplr_step(void* S, const void* r, const void* w, const void* k,

@@ -22,6 +22,7 @@
 #include "common.cuh"
 
 namespace {
+__device__ int g_chunk_bad = 0;  // a sequence / chunk table out of range (bit 2 of device_error)
 constexpr int CL = 16;                       // chunk length
 constexpr int KD = RWKV_HD;                  // 64
 constexpr int REC = 4 * CL * KD + KD + 2 * CL * CL;  // floats per (chunk, head) record
@@ -33,6 +34,7 @@ constexpr int RS = KD + 1;  // padded smem row stride (conflict-free column walk
 
 // chunk_cu[s] = number of chunks before sequence s (single block, S <= 65536).
 __global__ void k_chunk_table(const int* __restrict__ cu, int* __restrict__ chunk_cu, int S) {
+  RWKV_GRID_DEP_ENTRY();
   __shared__ int part[1024];
   const int tid = threadIdx.x;
   const int per = (S + blockDim.x - 1) / blockDim.x;
@@ -62,7 +64,8 @@ __global__ void k_chunk_table(const int* __restrict__ cu, int* __restrict__ chun
 __global__ void __launch_bounds__(256) k_chunk_prep(
     const __half* __restrict__ rb, const __half* __restrict__ wb, const __half* __restrict__ kb,
     const __half* __restrict__ ab, const __half* __restrict__ bb, const int* __restrict__ cu,
-    const int* __restrict__ chunk_cu, int S, int C, float* __restrict__ rec) {
+    const int* __restrict__ chunk_cu, int S, int C, int M, float* __restrict__ rec) {
+  RWKV_GRID_DEP_ENTRY();
   __shared__ float sa_[CL * RS], sb_[CL * RS], sk_[CL * RS], sr_[CL * RS], sg[CL * RS];
   __shared__ float Aab[CL][CL + 1], Aak[CL][CL + 1], Brb[CL][CL + 1], Brk[CL][CL + 1],
       Tm[CL][CL + 1], PU[CL][CL + 1];
@@ -81,6 +84,10 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
       const int m0 = cu[s] + (c - chunk_cu[s]) * CL;
       info[1] = m0;
       info[2] = min(CL, cu[s + 1] - m0);
+      if (m0 < 0 || info[2] <= 0 || m0 + info[2] > M) {
+        atomicExch(&g_chunk_bad, 1);
+        info[0] = 0;
+      }
     }
   }
   __syncthreads();
@@ -235,7 +242,8 @@ constexpr size_t SCAN_SMEM = (size_t)NSTAGE * (REC + CL * 8 / 2) * sizeof(float)
 __global__ void __launch_bounds__(256) k_chunk_scan(
     const __half* __restrict__ vbuf, const float* __restrict__ rec, const int* __restrict__ cu,
     const int* __restrict__ chunk_cu, const int* __restrict__ slots, float* __restrict__ rnn,
-    __half* __restrict__ ybuf, int C) {
+    __half* __restrict__ ybuf, int C, int M, int max_chunks, int n_slots) {
+  RWKV_GRID_DEP_ENTRY();
   extern __shared__ __align__(16) float scan_smem[];
   float* Rb = scan_smem;                                                   // [NSTAGE][REC]
   __half* Vb = reinterpret_cast<__half*>(scan_smem + (size_t)NSTAGE * REC);  // [NSTAGE][CL][8]
@@ -243,10 +251,15 @@ __global__ void __launch_bounds__(256) k_chunk_scan(
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = grp * 8 + warp;
   const int slot = slots ? slots[s] : s;
-  float* Srow = rnn + (((size_t)slot * H + h) * KD + row) * KD;
-  float2 st = *reinterpret_cast<const float2*>(Srow + 2 * lane);
   const int c0 = chunk_cu[s], c1 = chunk_cu[s + 1];
   const int m_beg = cu[s], m_end = cu[s + 1];
+  if (slot < 0 || slot >= n_slots || c0 < 0 || c1 < c0 || c1 > max_chunks || m_beg < 0 ||
+      m_end < m_beg || m_end > M || (m_end - m_beg + CL - 1) / CL != c1 - c0) {
+    if (tid == 0) atomicExch(&g_chunk_bad, 1);
+    return;
+  }
+  float* Srow = rnn + (((size_t)slot * H + h) * KD + row) * KD;
+  float2 st = *reinterpret_cast<const float2*>(Srow + 2 * lane);
   auto stage = [&](int c) {
     if (c < c1) {
       const int buf = (c - c0) % NSTAGE;
@@ -323,6 +336,7 @@ __global__ void k_wkv_epilogue(const __half* __restrict__ ybuf, const __half* __
                                const __half* __restrict__ gbuf, size_t plane,
                                const __half* __restrict__ r_k, const __half* __restrict__ lnx_w,
                                const __half* __restrict__ lnx_b, __half* __restrict__ yg, int C) {
+  RWKV_GRID_DEP_ENTRY();
   const int m = blockIdx.x, c = threadIdx.x * 2;
   const size_t o = (size_t)m * C + c;
   const float2 y = __half22float2(*reinterpret_cast<const __half2*>(ybuf + o));
@@ -362,13 +376,13 @@ size_t wkv_chunk_record_bytes(int M, int S, int H) {
 int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
                        const __half* a, const __half* b, float* rnn, const int* cu,
                        const int* slots, __half* ybuf, float* rec, int* chunk_cu, int M, int S,
-                       int H, cudaStream_t st) {
+                       int H, int n_slots, cudaStream_t st) {
   const int C = H * KD;
-  k_chunk_table<<<1, 1024, 0, st>>>(cu, chunk_cu, S);
-  int rc = rwkv_check_launch("chunk_table");
+  int rc = rwkv_launch("chunk_table", k_chunk_table, dim3(1), dim3(1024), 0, st, cu, chunk_cu, S);
   if (rc) return rc;
-  k_chunk_prep<<<dim3(M / CL + S, H), 256, 0, st>>>(r, w, k, a, b, cu, chunk_cu, S, C, rec);
-  if ((rc = rwkv_check_launch("chunk_prep"))) return rc;
+  if ((rc = rwkv_launch("chunk_prep", k_chunk_prep, dim3(M / CL + S, H), dim3(256), 0, st, r, w, k,
+                        a, b, cu, chunk_cu, S, C, M, rec)))
+    return rc;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -381,24 +395,31 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
     }
     attr_done[dev] = true;
   }
-  k_chunk_scan<<<dim3(S, H, KD / 8), 256, SCAN_SMEM, st>>>(v, rec, cu, chunk_cu, slots, rnn, ybuf,
-                                                          C);
-  return rwkv_check_launch("chunk_scan");
+  return rwkv_launch("chunk_scan", k_chunk_scan, dim3(S, H, KD / 8), dim3(256), SCAN_SMEM, st, v,
+                     rec, cu, chunk_cu, slots, rnn, ybuf, C, M, M / CL + S, n_slots);
 }
 
 int launch_wkv_epilogue(int sem, const __half* ybuf, const __half* rbuf, const __half* gbuf,
                         size_t plane, const __half* r_k, const __half* lnx_w,
                         const __half* lnx_b, __half* yg, int M, int C, cudaStream_t st) {
-  if (sem == SEM_DECODE)
-    k_wkv_epilogue<SEM_DECODE><<<M, C / 2, 0, st>>>(ybuf, rbuf, gbuf, plane, r_k, lnx_w, lnx_b, yg, C);
-  else
-    k_wkv_epilogue<SEM_PREFILL><<<M, C / 2, 0, st>>>(ybuf, rbuf, gbuf, plane, r_k, lnx_w, lnx_b, yg, C);
-  return rwkv_check_launch("wkv_epilogue");
+  return rwkv_launch("wkv_epilogue", sem == SEM_DECODE ? k_wkv_epilogue<SEM_DECODE> : k_wkv_epilogue<SEM_PREFILL>,
+                     dim3(M), dim3(C / 2), 0, st, ybuf, rbuf, gbuf, plane, r_k, lnx_w, lnx_b, yg, C);
 }
 
 __global__ void k_uniform_cu(int* cu, int S, int T) {
+  RWKV_GRID_DEP_ENTRY();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i <= S) cu[i] = i * T;
+}
+
+int wkv_chunk_bad_flag() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_chunk_bad, sizeof(int));
+  if (v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_chunk_bad, &z, sizeof(int));
+  }
+  return v;
 }
 
 extern "C" size_t rwkv7_dplr_chunked_workspace_bytes(int n_seq, int T, int H) {
@@ -411,6 +432,7 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
                                   const void* v, const void* a, const void* b, void* y, int n_seq,
                                   int T, int H, void* workspace, size_t workspace_bytes,
                                   void* stream) {
+  rwkv_chain_begin();
   if (!S || !r || !w || !k || !v || !a || !b || !y || n_seq <= 0 || T <= 0 || H <= 0) {
     rwkv_set_error("rwkv7_dplr_chunked: null pointer or bad size (n_seq=%d, T=%d, H=%d)", n_seq,
                    T, H);
@@ -431,12 +453,12 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
   int* chunk_cu = cu + n_seq + 1;
   float* rec = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                         (((size_t)(n_seq + 1) * 2 * sizeof(int) + 255) & ~size_t(255)));
-  k_uniform_cu<<<(n_seq + 256) / 256, 256, 0, st>>>(cu, n_seq, T);
-  int rc = rwkv_check_launch("uniform_cu");
+  int rc = rwkv_launch("uniform_cu", k_uniform_cu, dim3((n_seq + 256) / 256), dim3(256), 0, st, cu,
+                       n_seq, T);
   if (rc) return rc;
   return launch_wkv_chunked((const __half*)r, (const __half*)w, (const __half*)k,
                             (const __half*)v, (const __half*)a, (const __half*)b, (float*)S, cu,
-                            nullptr, (__half*)y, rec, chunk_cu, n_seq * T, n_seq, H, st);
+                            nullptr, (__half*)y, rec, chunk_cu, n_seq * T, n_seq, H, n_seq, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -463,6 +485,7 @@ static void* g_noalloc_ptr[64] = {};
 extern "C" int rwkv7_dplr_chunked_noalloc(void* S, const void* r, const void* w, const void* k,
                                           const void* v, const void* a, const void* b, void* y,
                                           int n_seq, int T, int H, void* stream) {
+  rwkv_chain_begin();
   if (n_seq <= 0 || T <= 0 || H <= 0) {
     rwkv_set_error("rwkv7_dplr_chunked_noalloc: bad size (n_seq=%d, T=%d, H=%d)", n_seq, T, H);
     return RWKV_ERR_ARG;

@@ -35,7 +35,8 @@ def _run(problems, epi):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 3072, 1024), (7, 288, 1024), (130, 1024, 4096),
-                                   (256, 65536, 1024), (4096, 4096, 1024), (33, 32, 64), (300, 1000, 128)])
+                                   (256, 65536, 1024), (4096, 4096, 1024), (33, 32, 64), (300, 1000, 128),
+                                   (256, 3072, 1024), (64, 1024, 4096), (256, 160, 1024)])
 def test_gemm_store(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
     A = torch.randn(M, K, device="cuda", generator=g).half()
