@@ -128,7 +128,8 @@ unsigned long long rwkv_b200_launch_count(void);
 /* Nonzero if, since the last call, a kernel on the current device gave up on a
  * bounded wait instead of spinning forever (bit 0 a GEMM pipeline barrier, bit 1 a
  * grid barrier of the persistent decode kernel), or a chunked-wkv kernel found a
- * sequence table out of range and skipped that sequence (bit 2). Reading clears it.
+ * sequence table out of range and skipped that sequence, or its scan gave up on a
+ * bounded wait for a chunk record (bit 2). Reading clears it.
  * Synchronous (reads device memory). */
 int rwkv_b200_device_error(void);
 
@@ -169,9 +170,9 @@ int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const void* k, con
 
 /* rwkv7_dplr_chunked for callers that cannot allocate device memory (a frozen
  * memory pool, a host framework that only hands out input/output buffers):
- * no workspace argument, no allocation. Its scratch is a fixed 16 MiB device
+ * no workspace argument, no allocation. Its scratch is a fixed 32 MiB device
  * array inside this library, so it accepts only problems whose
- * rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H) is at most 16 MiB and
+ * rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H) is at most 32 MiB and
  * returns RWKV_ERR_SPACE otherwise. The first call on a device looks up the
  * array's address (do it before any stream capture). All calls share the one
  * array: calls that overlap on the GPU (different streams) race. No

@@ -22,13 +22,17 @@
 #include "common.cuh"
 
 namespace {
-__device__ int g_chunk_bad = 0;  // a sequence / chunk table out of range (bit 2 of device_error)
+__device__ int g_chunk_bad = 0;  // 1: a sequence / chunk table out of range; 2: a scan wait gave up
 constexpr int CL = 16;                       // chunk length
 constexpr int KD = RWKV_HD;                  // 64
-constexpr int REC = 4 * CL * KD + KD + 2 * CL * CL;  // floats per (chunk, head) record
-// record layout (floats): What[CL][KD] | Q[CL][KD] | Bt[CL][KD] | Kt[CL][KD] | gL[KD] | PU[CL][CL] | PY[CL][CL]
-constexpr int OFF_W = 0, OFF_Q = CL * KD, OFF_B = 2 * CL * KD, OFF_K = 3 * CL * KD,
-              OFF_G = 4 * CL * KD, OFF_PU = 4 * CL * KD + KD, OFF_PY = OFF_PU + CL * CL;
+constexpr int RWS = 2 * CL + KD;             // per-row floats: PU v | PY v | U
+constexpr int SHARED_F = 3 * CL * KD + KD;    // row-independent part of a record
+constexpr int REC = SHARED_F + KD * RWS;      // floats per (chunk, head) record
+// record layout (floats): What[CL][KD] | Q[CL][KD] | Bt[CL][KD] | gL[KD] |
+//   per state row v: (PU v)[CL] | (PY v)[CL] | U[KD]   (the value-dependent terms, [KD][RWS])
+// with U = sum_j v_j Kt_j, the whole value input of the chunk to that state row.
+constexpr int OFF_W = 0, OFF_Q = CL * KD, OFF_B = 2 * CL * KD, OFF_G = 3 * CL * KD,
+              OFF_RW = SHARED_F;
 constexpr int RS = KD + 1;  // padded smem row stride (conflict-free column walks)
 }  // namespace
 
@@ -63,12 +67,14 @@ __global__ void k_chunk_table(const int* __restrict__ cu, int* __restrict__ chun
 // with identity transitions (w = 1, a = b = k = r = 0).
 __global__ void __launch_bounds__(256) k_chunk_prep(
     const __half* __restrict__ rb, const __half* __restrict__ wb, const __half* __restrict__ kb,
-    const __half* __restrict__ ab, const __half* __restrict__ bb, const int* __restrict__ cu,
+    const __half* __restrict__ vb, const __half* __restrict__ ab, const __half* __restrict__ bb,
+    const int* __restrict__ cu,
     const int* __restrict__ chunk_cu, int S, int C, int M, float* __restrict__ rec) {
   RWKV_GRID_DEP_ENTRY();
   __shared__ float sa_[CL * RS], sb_[CL * RS], sk_[CL * RS], sr_[CL * RS], sg[CL * RS];
   __shared__ float Aab[CL][CL + 1], Aak[CL][CL + 1], Brb[CL][CL + 1], Brk[CL][CL + 1],
-      Tm[CL][CL + 1], PU[CL][CL + 1];
+      Tm[CL][CL + 1], PU[CL][CL + 1], PY[CL][CL + 1];
+  __shared__ float sv_[CL * RS];
   __shared__ float Wh[CL * RS];
   __shared__ int info[3];
   const int c = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
@@ -97,11 +103,12 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
   // 1. load (fp16 -> fp32), pad
   for (int i = tid; i < CL * KD; i += 256) {
     const int t = i / KD, k = i % KD;
-    float r = 0.f, w = 1.f, kk = 0.f, a = 0.f, b = 0.f;
+    float r = 0.f, w = 1.f, kk = 0.f, vv = 0.f, a = 0.f, b = 0.f;
     if (t < n) {
       const size_t o = (size_t)(m0 + t) * C + hc + k;
-      r = h2f(rb[o]); w = h2f(wb[o]); kk = h2f(kb[o]); a = h2f(ab[o]); b = h2f(bb[o]);
+      r = h2f(rb[o]); w = h2f(wb[o]); kk = h2f(kb[o]); vv = h2f(vb[o]); a = h2f(ab[o]); b = h2f(bb[o]);
     }
+    sv_[t * RS + k] = vv;
     sr_[t * RS + k] = r; sg[t * RS + k] = logf(w); sk_[t * RS + k] = kk; sa_[t * RS + k] = a;
     sb_[t * RS + k] = b;
   }
@@ -167,7 +174,6 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
     float v = 0.f;
     for (int q = 0; q <= t; ++q) v += Tm[t][q] * Aak[q][j];
     PU[t][j] = v;
-    out[OFF_PU + t * CL + j] = v;
   }
   __syncthreads();
   // 6. Q = Rt + Brb What, PY = Brb PU + Brk, Bt/Kt/gL
@@ -178,155 +184,239 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
     out[OFF_Q + t * KD + k] = v;
     const float gl = expf(sg[(CL - 1) * RS + k]);
     out[OFF_B + t * KD + k] = sb_[t * RS + k] * gl;
-    out[OFF_K + t * KD + k] = sk_[t * RS + k] * gl;
     if (t == 0) out[OFF_G + k] = gl;
   }
   {
     const int t = tid >> 4, j = tid & 15;
     float v = Brk[t][j];
     for (int q = 0; q <= t; ++q) v += Brb[t][q] * PU[q][j];
-    out[OFF_PY + t * CL + j] = v;
+    PY[t][j] = v;
   }
-}
-
-// Sum 16 per-lane partials across the warp; lane l ends with the total of index (l >> 1) & 15.
-__device__ __forceinline__ float reduce16(float (&p)[16], int lane) {
+  __syncthreads();
+  // 7. the value-dependent terms per state row: (PU v)_t, (PY v)_t and U = sum_j v_j Kt_j
+  for (int i = tid; i < KD * CL; i += 256) {
+    const int row = i / CL, t = i % CL;
+    float pu = 0.f, py = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const bool up = lane & 16;
-    const float send = up ? p[i] : p[i + 8];
-    const float keep = up ? p[i + 8] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    for (int j = 0; j < CL; ++j) {
+      const float vj = sv_[j * RS + row];
+      pu += PU[t][j] * vj;
+      py += PY[t][j] * vj;
+    }
+    float* o = out + OFF_RW + row * RWS;
+    o[t] = pu;
+    o[CL + t] = py;
   }
+  for (int i = tid; i < KD * KD; i += 256) {
+    const int row = i / KD, k = i % KD;
+    float u = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const bool up = lane & 8;
-    const float send = up ? p[i] : p[i + 4];
-    const float keep = up ? p[i + 4] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    for (int j = 0; j < CL; ++j) u += sv_[j * RS + row] * sk_[j * RS + k];
+    out[OFF_RW + row * RWS + 2 * CL + k] = u * expf(sg[(CL - 1) * RS + k]);
   }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const bool up = lane & 4;
-    const float send = up ? p[i] : p[i + 2];
-    const float keep = up ? p[i + 2] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  {
-    const bool up = lane & 2;
-    const float send = up ? p[0] : p[1];
-    const float keep = up ? p[1] : p[0];
-    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-  return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src));
+// ---- chunk scan: bounded mbarrier waits and 1-D bulk copies ------------------------
+namespace {
+constexpr uint64_t SCAN_WAIT_NS = 200ull * 1000 * 1000;  // 200 ms: a bounded wait gave up
+__device__ __forceinline__ uint32_t sm_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void sc_mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sm_addr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void sc_mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm_addr(b)) : "memory");
+}
+__device__ __forceinline__ void sc_mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm_addr(b)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool sc_mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(sm_addr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for phase `parity` of b for at most SCAN_WAIT_NS; false (and the error flag) on expiry.
+__device__ __forceinline__ bool sc_mbar_wait(uint64_t* b, uint32_t parity) {
+  if (sc_mbar_try(b, parity)) return true;
+  const uint64_t t0 = gtimer();
+  while (!sc_mbar_try(b, parity)) {
+    if (gtimer() - t0 > SCAN_WAIT_NS) {
+      atomicOr(&g_chunk_bad, 2);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void sc_bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                            uint64_t* b) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          sm_addr(dst)),
+      "l"(src), "r"(bytes), "r"(sm_addr(b))
+      : "memory");
 }
 
-__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool pred) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
-  const int sz = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(sz));
+// 4-wide dot product with packed fp32 pairs.
+__device__ __forceinline__ float dot4(float4 a, float2 s01, float2 s23) {
+  const float2 p = __ffma2_rn(make_float2(a.z, a.w), s23, __fmul2_rn(make_float2(a.x, a.y), s01));
+  return p.x + p.y;
 }
 
-constexpr int NSTAGE = 4;  // chunk records in flight per CTA
-constexpr size_t SCAN_SMEM = (size_t)NSTAGE * (REC + CL * 8 / 2) * sizeof(float);
+constexpr int SCAN_ROWS = 8;                        // state rows per CTA
+constexpr int SCAN_THREADS = 128;                   // four warps, two rows each
+constexpr int SLICE_F = SCAN_ROWS * RWS;            // per-CTA part of a record's row terms
+constexpr int STAGE_F = SHARED_F + SLICE_F;         // floats per ring stage
+// Chunk records in flight per CTA. Eight stages (125 KB) also keep a second scan CTA
+// off the SM: placed early by programmatic dependent launch, CTAs could otherwise
+// pile up two or three per SM, and the slowest SM sets the scan's time.
+constexpr int NSTAGE = 8;
+constexpr size_t SCAN_SMEM = (size_t)NSTAGE * STAGE_F * sizeof(float) + 2 * NSTAGE * sizeof(uint64_t);
+static_assert((SHARED_F * 4) % 16 == 0 && (SLICE_F * 4) % 16 == 0 && (REC * 4) % 16 == 0,
+              "bulk copies need 16-byte multiples");
+static_assert(SCAN_SMEM > 114 * 1024 && SCAN_SMEM <= 227 * 1024, "one scan CTA per SM");
+}  // namespace
 
-// grid = (S, H, 8 row groups), block = 256: warp w owns state row v = 8 * group + w.
-// Chunk records (and the 16 x 8 values of v the CTA needs) stream through an
-// NSTAGE-deep cp.async ring, so each chunk only waits for its own math. y (fp16,
-// rounded like the reference's y store) goes to ybuf [M, C].
-__global__ void __launch_bounds__(256) k_chunk_scan(
-    const __half* __restrict__ vbuf, const float* __restrict__ rec, const int* __restrict__ cu,
-    const int* __restrict__ chunk_cu, const int* __restrict__ slots, float* __restrict__ rnn,
-    __half* __restrict__ ybuf, int C, int M, int max_chunks, int n_slots) {
+// grid = (S, H, KD / 8 row groups), block = 128. Each half-warp owns one state row
+// (lane l of the half holds keys 4l..4l+3 of it), so a warp carries two rows. Chunk
+// records stream through an NSTAGE ring of 1-D bulk copies (mbarrier full / empty).
+// Per chunk a half-warp forms the 16 What and 16 Q dot products of its row, reduces
+// the 32 partial sums across its 16 lanes (lane l ends with sums 2l and 2l + 1: the
+// in-chunk states sa for l < 8, the outputs y for l >= 8), adds the value terms
+// PU v / PY v that k_chunk_prep precomputed, writes y (fp16, rounded like the
+// reference's y store) to ybuf [M, C] and advances the fp32 state by
+//   s <- s * gL + sum_j sa_j Bt_j + U.
+__global__ void __launch_bounds__(SCAN_THREADS) k_chunk_scan(
+    const float* __restrict__ rec, const int* __restrict__ cu, const int* __restrict__ chunk_cu,
+    const int* __restrict__ slots, float* __restrict__ rnn, __half* __restrict__ ybuf, int C,
+    int M, int max_chunks, int n_slots) {
   RWKV_GRID_DEP_ENTRY();
-  extern __shared__ __align__(16) float scan_smem[];
-  float* Rb = scan_smem;                                                   // [NSTAGE][REC]
-  __half* Vb = reinterpret_cast<__half*>(scan_smem + (size_t)NSTAGE * REC);  // [NSTAGE][CL][8]
+  extern __shared__ __align__(128) float scan_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(scan_smem + (size_t)NSTAGE * STAGE_F);
+  uint64_t* empty = full + NSTAGE;
   const int s = blockIdx.x, h = blockIdx.y, H = gridDim.y, grp = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row = grp * 8 + warp;
+  const int hl = lane & 15, lrow = warp * 2 + (lane >> 4);
+  const int row = grp * SCAN_ROWS + lrow;
   const int slot = slots ? slots[s] : s;
   const int c0 = chunk_cu[s], c1 = chunk_cu[s + 1];
   const int m_beg = cu[s], m_end = cu[s + 1];
   if (slot < 0 || slot >= n_slots || c0 < 0 || c1 < c0 || c1 > max_chunks || m_beg < 0 ||
       m_end < m_beg || m_end > M || (m_end - m_beg + CL - 1) / CL != c1 - c0) {
-    if (tid == 0) atomicExch(&g_chunk_bad, 1);
+    if (tid == 0) atomicOr(&g_chunk_bad, 1);
     return;
   }
-  float* Srow = rnn + (((size_t)slot * H + h) * KD + row) * KD;
-  float2 st = *reinterpret_cast<const float2*>(Srow + 2 * lane);
-  auto stage = [&](int c) {
-    if (c < c1) {
-      const int buf = (c - c0) % NSTAGE;
-      const float* src = rec + ((size_t)c * H + h) * REC;
-      for (int i = tid; i < REC / 4; i += 256) cp_async16(Rb + (size_t)buf * REC + 4 * i, src + 4 * i);
-      if (tid < CL) {  // token tid's 8 values of v for this CTA's rows (zero past the end)
-        const int m = m_beg + (c - c0) * CL + tid;
-        const bool ok = m < m_end;
-        cp_async16_zfill(Vb + ((size_t)buf * CL + tid) * 8,
-                         vbuf + (size_t)(ok ? m : m_beg) * C + h * KD + grp * 8, ok);
-      }
+  if (tid == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      sc_mbar_init(&full[i], 1);
+      sc_mbar_init(&empty[i], SCAN_THREADS / 32);
     }
-    asm volatile("cp.async.commit_group;\n" ::);
-  };
-#pragma unroll
-  for (int i = 0; i < NSTAGE - 1; ++i) stage(c0 + i);
-  for (int c = c0; c < c1; ++c) {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(NSTAGE - 2));
-    __syncthreads();  // chunk c landed; every warp is done with chunk c - 1's buffer
-    stage(c + NSTAGE - 1);
-    const int buf = (c - c0) % NSTAGE;
-    const float* R = Rb + (size_t)buf * REC;
-    const float vt = lane < CL ? __half2float(Vb[((size_t)buf * CL + lane) * 8 + warp]) : 0.f;
-    const int m0 = m_beg + (c - c0) * CL;
-    const int n = min(CL, m_end - m0);
-    float pw[16], pq[16];
-#pragma unroll
-    for (int t = 0; t < CL; ++t) {
-      const float2 w2 = *reinterpret_cast<const float2*>(R + OFF_W + t * KD + 2 * lane);
-      const float2 q2 = *reinterpret_cast<const float2*>(R + OFF_Q + t * KD + 2 * lane);
-      pw[t] = w2.x * st.x + w2.y * st.y;
-      pq[t] = q2.x * st.x + q2.y * st.y;
-    }
-    // the P_U v / P_Y v terms join the partial sums before the reduction: lane j < 16
-    // holds v_j and adds column j of P_U / P_Y to every row's partial
-#pragma unroll
-    for (int t = 0; t < CL; ++t) {
-      if (lane < CL) {
-        pw[t] += R[OFF_PU + t * CL + lane] * vt;
-        pq[t] += R[OFF_PY + t * CL + lane] * vt;
-      }
-    }
-    const float sa = reduce16(pw, lane);
-    const float y = reduce16(pq, lane);
-    const int tt = (lane >> 1) & 15;
-    if ((lane & 1) == 0 && tt < n) ybuf[(size_t)(m0 + tt) * C + h * KD + row] = f2h(y);
-    const float2 gl = *reinterpret_cast<const float2*>(R + OFF_G + 2 * lane);
-    float2 n0 = make_float2(st.x * gl.x, st.y * gl.y), n1 = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int j = 0; j < CL; j += 2) {
-      const float sa0 = __shfl_sync(0xffffffffu, sa, 2 * j);
-      const float sa1 = __shfl_sync(0xffffffffu, sa, 2 * j + 2);
-      const float v0 = __shfl_sync(0xffffffffu, vt, j);
-      const float v1 = __shfl_sync(0xffffffffu, vt, j + 1);
-      const float2 b0 = *reinterpret_cast<const float2*>(R + OFF_B + j * KD + 2 * lane);
-      const float2 k0 = *reinterpret_cast<const float2*>(R + OFF_K + j * KD + 2 * lane);
-      const float2 b1 = *reinterpret_cast<const float2*>(R + OFF_B + (j + 1) * KD + 2 * lane);
-      const float2 k1 = *reinterpret_cast<const float2*>(R + OFF_K + (j + 1) * KD + 2 * lane);
-      n0.x += sa0 * b0.x + v0 * k0.x;
-      n0.y += sa0 * b0.y + v0 * k0.y;
-      n1.x += sa1 * b1.x + v1 * k1.x;
-      n1.y += sa1 * b1.y + v1 * k1.y;
-    }
-    st = make_float2(n0.x + n1.x, n0.y + n1.y);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  asm volatile("cp.async.wait_group 0;\n" ::);
-  *reinterpret_cast<float2*>(Srow + 2 * lane) = st;
+  __syncthreads();
+  float* Srow = rnn + (((size_t)slot * H + h) * KD + row) * KD + 4 * hl;
+  float4 st = *reinterpret_cast<const float4*>(Srow);
+  int issued = 0;  // chunks whose copies thread 0 has issued
+  auto issue = [&](int c) {
+    const int buf = (c - c0) % NSTAGE;
+    float* dst = scan_smem + (size_t)buf * STAGE_F;
+    const float* src = rec + ((size_t)c * H + h) * REC;
+    sc_mbar_expect_tx(&full[buf], STAGE_F * 4);
+    sc_bulk_g2s(dst, src, SHARED_F * 4, &full[buf]);
+    sc_bulk_g2s(dst + SHARED_F, src + OFF_RW + grp * SLICE_F, SLICE_F * 4, &full[buf]);
+    ++issued;
+  };
+  if (tid == 0)
+    for (int i = 0; i < NSTAGE && c0 + i < c1; ++i) issue(c0 + i);
+  bool ok = true;
+  for (int c = c0; c < c1; ++c) {
+    const int it = c - c0, buf = it % NSTAGE;
+    // refill the stage chunk c - 1 used, once all four warps are done with it
+    if (tid == 0 && it >= 1 && c - 1 + NSTAGE < c1) {
+      if (sc_mbar_wait(&empty[(it - 1) % NSTAGE], ((it - 1) / NSTAGE) & 1)) issue(c - 1 + NSTAGE);
+      else ok = false;
+    }
+    ok = __all_sync(0xffffffffu, ok && sc_mbar_wait(&full[buf], (it / NSTAGE) & 1));
+    if (!ok) break;
+    const float* R = scan_smem + (size_t)buf * STAGE_F;
+    const float* RW = R + SHARED_F + lrow * RWS;
+    const float2 s01 = make_float2(st.x, st.y), s23 = make_float2(st.z, st.w);
+    float p[32];
+#pragma unroll
+    for (int t = 0; t < CL; ++t) {
+      p[t] = dot4(*reinterpret_cast<const float4*>(R + OFF_W + t * KD + 4 * hl), s01, s23);
+      p[CL + t] = dot4(*reinterpret_cast<const float4*>(R + OFF_Q + t * KD + 4 * hl), s01, s23);
+    }
+    // transpose-reduce over the 16 lanes of the half-warp: 32 -> 16 -> 8 -> 4 -> 2 sums
+#pragma unroll
+    for (int m = 8, half = 16; m >= 1; m >>= 1, half >>= 1) {
+      const bool up = lane & m;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? p[i] : p[i + half];
+        const float keep = up ? p[i + half] : p[i];
+        p[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+      }
+    }
+    // lane hl holds sums 2hl, 2hl + 1: (What s)_t for hl < 8, (Q s)_t for hl >= 8, t = 2hl mod 16
+    const float2 add = *reinterpret_cast<const float2*>(RW + 2 * hl);
+    const float o0 = p[0] + add.x, o1 = p[1] + add.y;
+    if (hl >= 8) {
+      const int m0 = m_beg + it * CL + 2 * hl - CL;
+      __half* yp = ybuf + (size_t)m0 * C + h * KD + row;
+      if (m0 < m_end) yp[0] = f2h(o0);
+      if (m0 + 1 < m_end) yp[C] = f2h(o1);
+    }
+    const float4 gl = *reinterpret_cast<const float4*>(R + OFF_G + 4 * hl);
+    const float4 u = *reinterpret_cast<const float4*>(RW + 2 * CL + 4 * hl);
+    float2 n01 = __ffma2_rn(s01, make_float2(gl.x, gl.y), make_float2(u.x, u.y));
+    float2 n23 = __ffma2_rn(s23, make_float2(gl.z, gl.w), make_float2(u.z, u.w));
+    float2 m01 = make_float2(0.f, 0.f), m23 = make_float2(0.f, 0.f);
+    const int src = lane & 16;
+#pragma unroll
+    for (int j = 0; j < CL; ++j) {
+      const float sa = __shfl_sync(0xffffffffu, (j & 1) ? o1 : o0, src + (j >> 1));
+      const float4 b = *reinterpret_cast<const float4*>(R + OFF_B + j * KD + 4 * hl);
+      const float2 sa2 = make_float2(sa, sa);
+      if (j & 1) {
+        m01 = __ffma2_rn(sa2, make_float2(b.x, b.y), m01);
+        m23 = __ffma2_rn(sa2, make_float2(b.z, b.w), m23);
+      } else {
+        n01 = __ffma2_rn(sa2, make_float2(b.x, b.y), n01);
+        n23 = __ffma2_rn(sa2, make_float2(b.z, b.w), n23);
+      }
+    }
+    n01 = __fadd2_rn(n01, m01);
+    n23 = __fadd2_rn(n23, m23);
+    st = make_float4(n01.x, n01.y, n23.x, n23.y);
+    __syncwarp();
+    if (lane == 0) sc_mbar_arrive(&empty[buf]);
+  }
+  if (!ok) {
+    // leave no bulk copy in flight into this CTA's shared memory
+    if (tid == 0)
+      for (int i = 0; i < NSTAGE && issued > 0; ++i) {
+        const int c = c0 + issued - 1 - i;
+        if (c < c0) break;
+        const int k = c - c0;
+        sc_mbar_wait(&full[k % NSTAGE], (k / NSTAGE) & 1);
+      }
+    return;
+  }
+  *reinterpret_cast<float4*>(Srow) = st;
 }
 
 // Per-head GroupNorm + bonus + g gate on precomputed y (one warp per head and row).
@@ -381,7 +471,7 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   int rc = rwkv_launch("chunk_table", k_chunk_table, dim3(1), dim3(1024), 0, st, cu, chunk_cu, S);
   if (rc) return rc;
   if ((rc = rwkv_launch("chunk_prep", k_chunk_prep, dim3(M / CL + S, H), dim3(256), 0, st, r, w, k,
-                        a, b, cu, chunk_cu, S, C, M, rec)))
+                        v, a, b, cu, chunk_cu, S, C, M, rec)))
     return rc;
   static bool attr_done[64] = {};
   int dev = 0;
@@ -395,8 +485,8 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
     }
     attr_done[dev] = true;
   }
-  return rwkv_launch("chunk_scan", k_chunk_scan, dim3(S, H, KD / 8), dim3(256), SCAN_SMEM, st, v,
-                     rec, cu, chunk_cu, slots, rnn, ybuf, C, M, M / CL + S, n_slots);
+  return rwkv_launch("chunk_scan", k_chunk_scan, dim3(S, H, KD / SCAN_ROWS), dim3(SCAN_THREADS), SCAN_SMEM,
+                     st, rec, cu, chunk_cu, slots, rnn, ybuf, C, M, M / CL + S, n_slots);
 }
 
 int launch_wkv_epilogue(int sem, const __half* ybuf, const __half* rbuf, const __half* gbuf,
@@ -438,6 +528,10 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
                    T, H);
     return RWKV_ERR_ARG;
   }
+  if (reinterpret_cast<uintptr_t>(S) & 15) {
+    rwkv_set_error("rwkv7_dplr_chunked: S must be 16-byte aligned");
+    return RWKV_ERR_ARG;
+  }
   const size_t need = rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) {
     rwkv_set_error("rwkv7_dplr_chunked: workspace needs %zu bytes, 256-aligned (got %zu)", need,
@@ -470,12 +564,12 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
 // only hands out input/output buffers, a plugin loaded into a process whose
 // allocator is not reachable from this library). For them the scratch lives
 // in this file-scope array instead: every GPU that loads the library holds
-// these 16 MiB until the process exits. In host code `g_noalloc_scratch` is
+// these 32 MiB until the process exits. In host code `g_noalloc_scratch` is
 // only a host-side stand-in for the symbol, never a device address; the device
 // address comes from cudaGetSymbolAddress, once per device, on that device's
 // first call (make that first call before any stream capture).
 namespace {
-constexpr size_t NOALLOC_BYTES = (size_t)16 << 20;
+constexpr size_t NOALLOC_BYTES = (size_t)32 << 20;
 }
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
 

@@ -59,4 +59,4 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     rc = lib.rwkv7_dplr_chunked_noalloc(p, p, p, p, p, p, p, p, 64, 4096, 16,
                                         torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.RWKV_ERR_SPACE
-    assert b"16777216" in lib.rwkv_b200_last_error()
+    assert b"33554432" in lib.rwkv_b200_last_error()
