@@ -69,12 +69,14 @@ extern "C" unsigned long long rwkv_b200_launch_count(void) {
 int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* emb,
                      const __half* ln_w, const __half* ln_b, const __half* mix6,
                      const __half* state_x, const int* row_seq, const int* cu, const int* slots,
-                     __half* xmix, __half* xlast, int M, int C, cudaStream_t st);
-int launch_cmix_rows(int sem, const __half* x, const __half* ln_w, const __half* ln_b,
+                     __half* xmix, __half* xlast, int M, int C, PendingResid pend,
+                     cudaStream_t st);
+int launch_cmix_rows(int sem, __half* x, const __half* ln_w, const __half* ln_b,
                      const __half* mu, const __half* state_x, const int* row_seq, const int* cu,
-                     const int* slots, __half* xk, __half* xlast, int M, int C, cudaStream_t st);
+                     const int* slots, __half* xk, __half* xlast, int M, int C, PendingResid pend,
+                     cudaStream_t st);
 int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __half* b,
-                   __half* out, int n, int C, cudaStream_t st);
+                   __half* out, int n, int M, int C, PendingResid pend, cudaStream_t st);
 int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,
                            int S, int L, int n_slots, int C, cudaStream_t st);
 int launch_gates_ew(int sem, const void* lora, const __half* rkv, const __half* w0,
@@ -85,7 +87,7 @@ int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t pl
                       const int* cu, const int* slots, __half* yg, int n_seqs, int H, int C,
                       cudaStream_t st);
 int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
-                   size_t ws_floats, cudaStream_t st);
+                   size_t ws_floats, cudaStream_t st, int* splits_out = nullptr);
 size_t wkv_chunk_record_bytes(int M, int S, int H);
 int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
                        const __half* a, const __half* b, float* rnn, const int* cu,
@@ -240,6 +242,12 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   if (cudaMemsetAsync(w.ranks, 0, (size_t)M * RANKS_LD * sizeof(__half), st) != cudaSuccess)
     return rwkv_check_launch("ranks memset");
 
+  // The residual GEMMs (W_o, FFN value) leave a split-K reduce to the next row kernel
+  // (cmix_rows / the next layer's tmix_rows / ln_rows), which needs the sum anyway.
+  PendingResid pend{nullptr, nullptr, 0};
+  auto defer = [&](int splits, const __half* res) {
+    pend = splits > 1 ? PendingResid{w.splitk, res, splits} : PendingResid{nullptr, nullptr, 0};
+  };
   for (int l = 0; l < L; ++l) {
     const rwkv7_layer& Lw = model->layers[l];
     const __half* wrkv = (const __half*)Lw.w_rkv;
@@ -253,7 +261,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
     // ---- TMIX ----
     TRY(launch_tmix_rows(sem, w.x, l == 0 ? b->tokens : nullptr, emb, (const __half*)Lw.ln1_w,
                          (const __half*)Lw.ln1_b, (const __half*)Lw.mix6, st_tx, b->row_seq,
-                         b->cu_seqlens, b->slots, w.xmix, xl_t, M, C, st));
+                         b->cu_seqlens, b->slots, w.xmix, xl_t, M, C, pend, st));
     {
       // r/k/v projections: xmix planes r=0, k=2, v=3
       rwkv7_gemm_problem p[3] = {
@@ -305,24 +313,28 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
                             b->cu_seqlens, b->slots, w.yg, S, H, C, st));
     {
       rwkv7_gemm_problem p = {w.yg, Lw.w_o, w.x1, w.x, M, C, C, C, C, C};
-      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RESID, w.splitk, w.splitk_floats, st));
+      int splits = 1;
+      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RESID, w.splitk, w.splitk_floats, st, &splits));
+      defer(splits, w.x);
     }
     // ---- CMIX ----
     TRY(launch_cmix_rows(sem, w.x1, (const __half*)Lw.ln2_w, (const __half*)Lw.ln2_b,
                          (const __half*)Lw.ffn_x_k, st_cx, b->row_seq, b->cu_seqlens, b->slots,
-                         w.xk, xl_c, M, C, st));
+                         w.xk, xl_c, M, C, pend, st));
     {
       rwkv7_gemm_problem p = {w.xk, Lw.w_fk, w.h, nullptr, M, 4 * C, C, C, C, 4 * C};
       TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RELUSQ, w.splitk, w.splitk_floats, st));
     }
     {
       rwkv7_gemm_problem p = {w.h, Lw.w_fv, w.x, w.x1, M, C, 4 * C, 4 * C, 4 * C, C};
-      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RESID, w.splitk, w.splitk_floats, st));
+      int splits = 1;
+      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_RESID, w.splitk, w.splitk_floats, st, &splits));
+      defer(splits, w.x1);
     }
   }
   if (b->n_logits) {
     TRY(launch_ln_rows(w.x, b->logit_rows, (const __half*)model->lnout_w,
-                       (const __half*)model->lnout_b, w.lnout, b->n_logits, C, st));
+                       (const __half*)model->lnout_b, w.lnout, b->n_logits, M, C, pend, st));
     rwkv7_gemm_problem p = {w.lnout, model->head, b->logits, nullptr, b->n_logits, model->vocab,
                             C, C, C, model->vocab};
     TRY(gemm_launch_ws(&p, 1, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));

@@ -126,6 +126,14 @@ __device__ __forceinline__ void grid_dep_trigger() {
     grid_dep_trigger();       \
   } while (0)
 
+// A residual sum res + A @ B whose split-K GEMM left its `splits` fp32 K-slices in
+// ws ([splits][M][C]) for the consuming row kernel to finish; ws == nullptr: none.
+struct PendingResid {
+  const float* ws;
+  const __half* res;
+  int splits;
+};
+
 bool rwkv_pdl_enabled();  // RWKV_B200_PDL=0 turns the attribute off (plain stream order)
 // Start of a library call: its first launch depends on whatever the caller queued
 // before (copies, memsets, other libraries' kernels) in plain stream order; only

@@ -212,21 +212,26 @@ int gemm_mma_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStre
 
 bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n);
 int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_t ws_floats,
-                   cudaStream_t st);
+                   cudaStream_t st, int* splits_out);
 
 // Kernel choice by shape: the tcgen05 kernel when every problem has K % 64 == 0
 // (all model projections; it picks its tile shape and split-K itself, `ws` being
 // the split-K scratch), else the mma.sync kernel. RWKV_B200_GEMM=mma|tc forces one.
+// With `splits_out` non-null a split-K GEMM leaves its fp32 K-slices in ws for the
+// consumer to sum (*splits_out > 1) instead of launching the reduce.
 int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
-                   size_t ws_floats, cudaStream_t st) {
+                   size_t ws_floats, cudaStream_t st, int* splits_out) {
   const char* e = getenv("RWKV_B200_GEMM");
   const bool force_mma = e && e[0] == 'm';
-  if (force_mma || !gemm_tc_eligible(problems, n)) return gemm_mma_launch(problems, n, epi, st);
-  return gemm_tc_launch(problems, n, epi, ws, ws_floats, st);
+  if (force_mma || !gemm_tc_eligible(problems, n)) {
+    if (splits_out) *splits_out = 1;
+    return gemm_mma_launch(problems, n, epi, st);
+  }
+  return gemm_tc_launch(problems, n, epi, ws, ws_floats, st, splits_out);
 }
 
 int gemm_launch(const rwkv7_gemm_problem* problems, int n, int epi, cudaStream_t st) {
-  return gemm_launch_ws(problems, n, epi, nullptr, 0, st);
+  return gemm_launch_ws(problems, n, epi, nullptr, 0, st, nullptr);
 }
 
 extern "C" int rwkv7_gemm_f16(const rwkv7_gemm_problem* problems, int n_problems, int epilogue,

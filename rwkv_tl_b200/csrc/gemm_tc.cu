@@ -466,15 +466,18 @@ bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n) {
 
 template <int BN, int STAGES>
 int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
-                       cudaStream_t st);
+                       bool defer, cudaStream_t st);
 
 // Tile configuration and split-K by problem size. Large grids: 128 x 128 tiles,
 // 3 stages (two CTAs per SM). Small grids (batched decode): 128 x 64 tiles with 6
 // stages (144 KiB of operands in flight per CTA) and, when still fewer than 48
 // tiles, a K split with at least 8 K-blocks per slice. `ws` takes the split-K fp32
-// partial tiles (ws_floats floats; no initial value needed).
+// partial tiles (ws_floats floats; no initial value needed). With `splits_out`
+// non-null the split-K reduce is left to the consumer: *splits_out receives the
+// number of K-slices parked in ws ([splits][M][N] fp32 per problem, problems back to
+// back), 1 when the GEMM wrote its output directly.
 int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_t ws_floats,
-                   cudaStream_t st) {
+                   cudaStream_t st, int* splits_out) {
   int tiles128 = 0, tiles64 = 0, min_kb = 1 << 30;
   size_t mn = 0;
   bool n4 = true;
@@ -485,18 +488,20 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_
     mn += (size_t)p[i].M * p[i].N;
     n4 = n4 && p[i].N % 4 == 0 && p[i].ldc % 2 == 0;
   }
-  if (tiles128 >= 148) return gemm_tc_launch_cfg<128, 3>(p, n, epi, 1, ws, st);
+  if (splits_out) *splits_out = 1;
+  if (tiles128 >= 148) return gemm_tc_launch_cfg<128, 3>(p, n, epi, 1, ws, false, st);
   int splits = 1;
   if (ws && n4 && tiles64 < 48) {
     splits = max(1, min(min_kb / 8, (128 + tiles64 - 1) / tiles64));
     while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
   }
-  return gemm_tc_launch_cfg<64, 6>(p, n, epi, splits, ws, st);
+  if (splits_out) *splits_out = splits;
+  return gemm_tc_launch_cfg<64, 6>(p, n, epi, splits, ws, splits_out != nullptr, st);
 }
 
 template <int BN, int STAGES>
 int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
-                       cudaStream_t st) {
+                       bool defer, cudaStream_t st) {
   TcParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.n_problems = n;
@@ -531,7 +536,7 @@ int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, 
     case RWKV_EPI_LORA_ACT: rc = launch_tc<BN, RWKV_EPI_LORA_ACT, STAGES>(prm, grid, st); break;
     default: rc = launch_tc<BN, RWKV_EPI_LORA_ACT2, STAGES>(prm, grid, st); break;
   }
-  if (rc || splits == 1) return rc;
+  if (rc || splits == 1 || defer) return rc;
   ReduceParams rp;
   rp.n_problems = n;
   rp.splits = splits;

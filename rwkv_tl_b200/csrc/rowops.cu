@@ -51,6 +51,21 @@ __device__ __forceinline__ float4 lerp4(float4 x, float4 p, float4 mu) {
                      lerp_sem<SEM>(x.z, p.z, mu.z), lerp_sem<SEM>(x.w, p.w, mu.w));
 }
 
+// Row m, channels c..c+3, of a residual sum whose split-K reduce was left to this
+// kernel: fp16(res + fp16(sum_s ws[s])), slices summed in split order -- the same
+// values the GEMM's residual epilogue (RWKV_EPI_RESID) stores after its reduce.
+__device__ __forceinline__ float4 pending_row4(const PendingResid& p, int m, int c, int M, int C) {
+  const size_t i = (size_t)m * C + c, MC = (size_t)M * C;
+  float4 acc = __ldcg(reinterpret_cast<const float4*>(p.ws + i));
+  for (int s = 1; s < p.splits; ++s) {
+    const float4 q = __ldcg(reinterpret_cast<const float4*>(p.ws + s * MC + i));
+    acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+  }
+  const float4 r = load_h4(p.res + i);
+  return make_float4(r16(r.x + r16(acc.x)), r16(r.y + r16(acc.y)), r16(r.z + r16(acc.z)),
+                     r16(r.w + r16(acc.w)));
+}
+
 }  // namespace
 
 // TMIX input stage: [embedding gather] + LN1 + token shift + 6 lerps.
@@ -63,7 +78,8 @@ __global__ void k_tmix_rows(__half* __restrict__ x, const int64_t* __restrict__ 
                             const __half* __restrict__ ln_b, const __half* __restrict__ mix6,
                             const __half* __restrict__ state_x, const int* __restrict__ row_seq,
                             const int* __restrict__ cu, const int* __restrict__ slots,
-                            __half* __restrict__ xmix, __half* __restrict__ xlast, int M, int C) {
+                            __half* __restrict__ xmix, __half* __restrict__ xlast, int M, int C,
+                            const PendingResid pend) {
   RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32 * 2];
   const int m = blockIdx.x, c = threadIdx.x * 4;
@@ -73,6 +89,10 @@ __global__ void k_tmix_rows(__half* __restrict__ x, const int64_t* __restrict__ 
   if (tokens) {
     v[0] = load_h4(emb + (size_t)tokens[m] * C + c);
     v[1] = first ? v[0] : load_h4(emb + (size_t)tokens[m - 1] * C + c);
+    store_h4(x + (size_t)m * C + c, v[0]);
+  } else if (pend.ws) {  // x = res + (split-K GEMM output), finished here
+    v[0] = pending_row4(pend, m, c, M, C);
+    v[1] = first ? v[0] : pending_row4(pend, m - 1, c, M, C);
     store_h4(x + (size_t)m * C + c, v[0]);
   } else {
     v[0] = load_h4(x + (size_t)m * C + c);
@@ -90,19 +110,26 @@ __global__ void k_tmix_rows(__half* __restrict__ x, const int64_t* __restrict__ 
 
 // CMIX input stage: LN2 + token shift + one lerp (x_k).
 template <int SEM>
-__global__ void k_cmix_rows(const __half* __restrict__ x, const __half* __restrict__ ln_w,
+__global__ void k_cmix_rows(__half* __restrict__ x, const __half* __restrict__ ln_w,
                             const __half* __restrict__ ln_b, const __half* __restrict__ mu,
                             const __half* __restrict__ state_x, const int* __restrict__ row_seq,
                             const int* __restrict__ cu, const int* __restrict__ slots,
-                            __half* __restrict__ xk, __half* __restrict__ xlast, int C) {
+                            __half* __restrict__ xk, __half* __restrict__ xlast, int M, int C,
+                            const PendingResid pend) {
   RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32 * 2];
   const int m = blockIdx.x, c = threadIdx.x * 4;
   const int s = row_seq[m];
   const bool first = (m == cu[s]), last = (m == cu[s + 1] - 1);
   float4 v[2];
-  v[0] = load_h4(x + (size_t)m * C + c);
-  v[1] = first ? v[0] : load_h4(x + (size_t)(m - 1) * C + c);
+  if (pend.ws) {  // x = res + (split-K GEMM output), finished here
+    v[0] = pending_row4(pend, m, c, M, C);
+    v[1] = first ? v[0] : pending_row4(pend, m - 1, c, M, C);
+    store_h4(x + (size_t)m * C + c, v[0]);
+  } else {
+    v[0] = load_h4(x + (size_t)m * C + c);
+    v[1] = first ? v[0] : load_h4(x + (size_t)(m - 1) * C + c);
+  }
   ln_rows<2>(v, ln_w, ln_b, c, C, red);
   const int slot = slots ? slots[s] : s;
   const float4 prev = first ? load_h4(state_x + (size_t)slot * C + c) : v[1];
@@ -113,12 +140,12 @@ __global__ void k_cmix_rows(const __half* __restrict__ x, const __half* __restri
 // ln_out of the rows that produce logits: out[i] = LN(x[rows[i]]).
 __global__ void k_ln_rows(const __half* __restrict__ x, const int* __restrict__ rows,
                           const __half* __restrict__ w, const __half* __restrict__ b,
-                          __half* __restrict__ out, int C) {
+                          __half* __restrict__ out, int M, int C, const PendingResid pend) {
   RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32];
   const int i = blockIdx.x, c = threadIdx.x * 4;
   float4 v[1];
-  v[0] = load_h4(x + (size_t)rows[i] * C + c);
+  v[0] = pend.ws ? pending_row4(pend, rows[i], c, M, C) : load_h4(x + (size_t)rows[i] * C + c);
   ln_rows<1>(v, w, b, c, C, red);
   store_h4(out + (size_t)i * C + c, v[0]);
 }
@@ -139,24 +166,27 @@ __global__ void k_scatter_state_x(const __half* __restrict__ xlast, __half* __re
 int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* emb,
                      const __half* ln_w, const __half* ln_b, const __half* mix6,
                      const __half* state_x, const int* row_seq, const int* cu, const int* slots,
-                     __half* xmix, __half* xlast, int M, int C, cudaStream_t st) {
+                     __half* xmix, __half* xlast, int M, int C, PendingResid pend,
+                     cudaStream_t st) {
   return rwkv_launch("tmix_rows", sem == SEM_DECODE ? k_tmix_rows<SEM_DECODE> : k_tmix_rows<SEM_PREFILL>,
                      dim3(M), dim3(C / 4), 0, st, x, tokens, emb, ln_w, ln_b, mix6, state_x, row_seq,
-                     cu, slots, xmix, xlast, M, C);
+                     cu, slots, xmix, xlast, M, C, pend);
 }
 
-int launch_cmix_rows(int sem, const __half* x, const __half* ln_w, const __half* ln_b,
+int launch_cmix_rows(int sem, __half* x, const __half* ln_w, const __half* ln_b,
                      const __half* mu, const __half* state_x, const int* row_seq, const int* cu,
-                     const int* slots, __half* xk, __half* xlast, int M, int C, cudaStream_t st) {
+                     const int* slots, __half* xk, __half* xlast, int M, int C, PendingResid pend,
+                     cudaStream_t st) {
   return rwkv_launch("cmix_rows", sem == SEM_DECODE ? k_cmix_rows<SEM_DECODE> : k_cmix_rows<SEM_PREFILL>,
                      dim3(M), dim3(C / 4), 0, st, x, ln_w, ln_b, mu, state_x, row_seq, cu, slots, xk,
-                     xlast, C);
+                     xlast, M, C, pend);
 }
 
 int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __half* b,
-                   __half* out, int n, int C, cudaStream_t st) {
+                   __half* out, int n, int M, int C, PendingResid pend, cudaStream_t st) {
   if (n == 0) return RWKV_OK;
-  return rwkv_launch("ln_rows", k_ln_rows, dim3(n), dim3(C / 4), 0, st, x, rows, w, b, out, C);
+  return rwkv_launch("ln_rows", k_ln_rows, dim3(n), dim3(C / 4), 0, st, x, rows, w, b, out, M, C,
+                     pend);
 }
 
 int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,
