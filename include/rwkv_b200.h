@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define RWKV_B200_ABI_VERSION 1
+#define RWKV_B200_ABI_VERSION 2
 
 enum {
   RWKV_OK = 0,
@@ -116,8 +116,16 @@ typedef struct rwkv7_batch {
   const int* slots;         /* [n_seqs] or NULL                                 */
   int n_logits;             /* rows that produce logits (0: state update only)  */
   const int* logit_rows;    /* [n_logits] row indices                           */
-  void* logits;             /* fp16 [n_logits, V]                               */
+  void* logits;             /* fp16 [n_logits, V], or NULL                      */
   int semantics;            /* RWKV_SEM_DECODE or RWKV_SEM_PREFILL              */
+  int64_t* next_ids;        /* [n_logits] greedy next token of each logit row,
+                               or NULL. The head GEMM then reduces each row to
+                               its argmax (lowest id among equal fp16 logits,
+                               like torch.argmax) in its epilogue: no logits are
+                               stored unless `logits` is also given. At least
+                               one of logits / next_ids when n_logits > 0.
+                               Replaces head @ x followed by the sampler's argmax
+                               (demo/_rwkv7_base.py:86-87, demo/sampling.py:13-70) */
 } rwkv7_batch;
 
 const char* rwkv_b200_last_error(void);

@@ -5,6 +5,7 @@ Public API (mirrors yuyi2439/rwkv-tl's ``demo`` + ``rwkv_tl`` names):
 ``BatchedState``, ``RWKV7Weight``, ``sample_logits``.
 """
 
+from . import ops  # registers torch.ops.rwkv_b200::*
 from .cuda_graph import CUDAGraph, make_graph_cls
 from .factory import make_rwkv7
 from .model import RWKV7B200, RWKV7Model
@@ -15,5 +16,5 @@ from .weight import RWKV7Weight
 
 __all__ = [
     "BatchedState", "ContinuousBatcher", "CUDAGraph", "RWKV7B200", "RWKV7Model", "RWKV7Weight",
-    "Request", "State", "make_graph_cls", "make_rwkv7", "sample_logits",
+    "Request", "State", "make_graph_cls", "make_rwkv7", "ops", "sample_logits",
 ]

@@ -73,7 +73,7 @@ class Batch(C.Structure):
         ("n_rows", C.c_int), ("n_seqs", C.c_int),
         ("tokens", vp), ("cu_seqlens", vp), ("row_seq", vp), ("slots", vp),
         ("n_logits", C.c_int), ("logit_rows", vp), ("logits", vp),
-        ("semantics", C.c_int),
+        ("semantics", C.c_int), ("next_ids", vp),
     ]
 
 
@@ -127,7 +127,7 @@ def load() -> C.CDLL:
     lib.rwkv7_decode_gemv.restype = C.c_int
     lib.rwkv7_decode_gemv.argtypes = [C.POINTER(Model), vp, C.c_int, vp, C.POINTER(StateDesc),
                                       vp, vp, C.c_size_t, vp]
-    if lib.rwkv_b200_abi_version() != 1:
+    if lib.rwkv_b200_abi_version() != 2:
         raise RWKVError("librwkv_b200.so ABI version mismatch")
     _lib = lib
     return lib

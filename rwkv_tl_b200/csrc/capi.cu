@@ -77,6 +77,7 @@ int launch_cmix_rows(int sem, __half* x, const __half* ln_w, const __half* ln_b,
                      cudaStream_t st);
 int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __half* b,
                    __half* out, int n, int M, int C, PendingResid pend, cudaStream_t st);
+int launch_argmax_finish(const unsigned long long* keys, int64_t* ids, int n, cudaStream_t st);
 int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,
                            int S, int L, int n_slots, int C, cudaStream_t st);
 int launch_gates_ew(int sem, const void* lora, const __half* rkv, const __half* w0,
@@ -120,6 +121,7 @@ struct Work {
   void* lora;  // 4 x [M, C] LoRA up outputs (fp32 decode semantics, fp16 prefill)
   float* chunk_rec;
   int* chunk_cu;
+  unsigned long long* argmax_keys;  // [n_logits] greedy-head keys (zero between calls)
   float* splitk;       // split-K partial tiles for small-M GEMMs
   size_t splitk_floats;
 };
@@ -153,6 +155,7 @@ Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) 
   w.h = c.take<__half>(4 * MC);
   w.xlast = c.take<__half>((size_t)L * 2 * S * C);
   w.lnout = c.take<__half>((size_t)n_logits * C);
+  w.argmax_keys = c.take<unsigned long long>((size_t)n_logits);
   w.chunk_cu = c.take<int>((size_t)S + 1);
   w.chunk_rec = c.take<float>(wkv_chunk_record_bytes(M, S, C / RWKV_HD) / sizeof(float));
   w.splitk_floats = splitk_floats(M, C);
@@ -212,7 +215,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   }
   const int M = b->n_rows, S = b->n_seqs, L = model->n_layer, C = model->n_embd, H = C / RWKV_HD;
   if (M <= 0 || S <= 0 || S > M || !b->tokens || !b->cu_seqlens || !b->row_seq ||
-      b->n_logits < 0 || (b->n_logits && (!b->logit_rows || !b->logits)) ||
+      b->n_logits < 0 || (b->n_logits && (!b->logit_rows || (!b->logits && !b->next_ids))) ||
       (b->semantics != RWKV_SEM_DECODE && b->semantics != RWKV_SEM_PREFILL) ||
       (!b->slots && S > state->n_slots)) {
     rwkv_set_error("rwkv7_forward: bad batch (rows=%d seqs=%d logits=%d semantics=%d)", M, S,
@@ -335,9 +338,21 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   if (b->n_logits) {
     TRY(launch_ln_rows(w.x, b->logit_rows, (const __half*)model->lnout_w,
                        (const __half*)model->lnout_b, w.lnout, b->n_logits, M, C, pend, st));
-    rwkv7_gemm_problem p = {w.lnout, model->head, b->logits, nullptr, b->n_logits, model->vocab,
-                            C, C, C, model->vocab};
-    TRY(gemm_launch_ws(&p, 1, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
+    if (b->logits) {
+      rwkv7_gemm_problem p = {w.lnout, model->head, b->logits, nullptr, b->n_logits,
+                              model->vocab, C, C, C, model->vocab};
+      TRY(gemm_launch_ws(&p, 1, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
+    }
+    if (b->next_ids) {
+      // greedy head: per-row argmax folded into the GEMM epilogue, no logits stored
+      if (cudaMemsetAsync(w.argmax_keys, 0, (size_t)b->n_logits * 8, st) != cudaSuccess)
+        return rwkv_check_launch("argmax key memset");
+      rwkv_chain_begin();  // the GEMM after the memset starts a plain-order chain
+      rwkv7_gemm_problem p = {w.lnout, model->head, w.argmax_keys, nullptr, b->n_logits,
+                              model->vocab, C, C, C, model->vocab};
+      TRY(gemm_launch_ws(&p, 1, EPI_ARGMAX, nullptr, 0, st));
+      TRY(launch_argmax_finish(w.argmax_keys, b->next_ids, b->n_logits, st));
+    }
   }
   TRY(launch_scatter_state_x(w.xlast, (__half*)state->tmix_x, (__half*)state->cmix_x, b->slots, S,
                              L, ns, C, st));

@@ -126,6 +126,18 @@ __device__ __forceinline__ void grid_dep_trigger() {
     grid_dep_trigger();       \
   } while (0)
 
+// Internal GEMM epilogue of the lm head's greedy path: C is a uint64 [M] array of
+// per-row keys (ordered fp16 logit << 32 | ~column), combined with atomicMax.
+constexpr int EPI_ARGMAX = 6;
+
+// Monotonic 64-bit key of (fp16-rounded value, column): a larger key is a larger
+// value, and among equal values the smaller column (torch.argmax picks the first).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int col) {
+  uint32_t u = __float_as_uint(v == 0.f ? 0.f : v);  // -0 and +0 compare equal
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (0xFFFFFFFFu - (uint32_t)col);
+}
+
 // A residual sum res + A @ B whose split-K GEMM left its `splits` fp32 K-slices in
 // ws ([splits][M][C]) for the consuming row kernel to finish; ws == nullptr: none.
 struct PendingResid {

@@ -239,6 +239,10 @@ extern "C" int rwkv7_gemm_f16(const rwkv7_gemm_problem* problems, int n_problems
   rwkv_chain_begin();
   int rc = gemm_validate(problems, n_problems);
   if (rc) return rc;
+  if (epilogue < RWKV_EPI_STORE || epilogue > RWKV_EPI_LORA_ACT2) {
+    rwkv_set_error("rwkv7_gemm_f16: unknown epilogue %d", epilogue);
+    return RWKV_ERR_ARG;
+  }
   for (int i = 0; i < n_problems; ++i)
     if (epilogue == RWKV_EPI_RESID && !problems[i].R) {
       rwkv_set_error("rwkv7_gemm_f16: residual epilogue needs R (problem %d)", i);

@@ -286,7 +286,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
     const __half* R = static_cast<const __half*>(P.R);
     const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
     const bool all_ok = __all_sync(0xffffffffu, ok);
-    if (!P.ws) {
+    if (!P.ws && EPI == EPI_ARGMAX) {
+      // greedy lm head: this tile's best (fp16 logit, lowest column) of the row
+      if (all_ok) {
+        unsigned long long best = 0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(trow + c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int col = n0 + c0 + i;
+            if (col < P.N) {
+              const unsigned long long key = argmax_key(r16(v[i]), col);
+              best = key > best ? key : best;
+            }
+          }
+        }
+        if (row < P.M) atomicMax(static_cast<unsigned long long*>(C) + row, best);
+      }
+    } else if (!P.ws) {
       if (all_ok) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -491,7 +510,7 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_
   if (splits_out) *splits_out = 1;
   if (tiles128 >= 148) return gemm_tc_launch_cfg<128, 3>(p, n, epi, 1, ws, false, st);
   int splits = 1;
-  if (ws && n4 && tiles64 < 48) {
+  if (ws && n4 && tiles64 < 48 && epi != EPI_ARGMAX) {
     splits = max(1, min(min_kb / 8, (128 + tiles64 - 1) / tiles64));
     while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
   }
@@ -534,6 +553,7 @@ int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, 
     case RWKV_EPI_RELUSQ: rc = launch_tc<BN, RWKV_EPI_RELUSQ, STAGES>(prm, grid, st); break;
     case RWKV_EPI_STORE_F32: rc = launch_tc<BN, RWKV_EPI_STORE_F32, STAGES>(prm, grid, st); break;
     case RWKV_EPI_LORA_ACT: rc = launch_tc<BN, RWKV_EPI_LORA_ACT, STAGES>(prm, grid, st); break;
+    case EPI_ARGMAX: rc = launch_tc<BN, EPI_ARGMAX, STAGES>(prm, grid, st); break;
     default: rc = launch_tc<BN, RWKV_EPI_LORA_ACT2, STAGES>(prm, grid, st); break;
   }
   if (rc || splits == 1 || defer) return rc;

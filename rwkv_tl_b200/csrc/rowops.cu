@@ -150,6 +150,15 @@ __global__ void k_ln_rows(const __half* __restrict__ x, const int* __restrict__ 
   store_h4(out + (size_t)i * C + c, v[0]);
 }
 
+// Greedy ids from the head GEMM's per-row keys (EPI_ARGMAX).
+__global__ void k_argmax_finish(const unsigned long long* __restrict__ keys, int64_t* __restrict__ ids,
+                                int n) {
+  RWKV_GRID_DEP_ENTRY();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  ids[i] = (int64_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
+}
+
 // New state x of every layer: tmix_x[l][slot] = xlast[l][0][s], cmix_x[l][slot] = xlast[l][1][s].
 // grid = (S, L, 2), block = C/4.
 __global__ void k_scatter_state_x(const __half* __restrict__ xlast, __half* __restrict__ tmix_x,
@@ -187,6 +196,11 @@ int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __ha
   if (n == 0) return RWKV_OK;
   return rwkv_launch("ln_rows", k_ln_rows, dim3(n), dim3(C / 4), 0, st, x, rows, w, b, out, M, C,
                      pend);
+}
+
+int launch_argmax_finish(const unsigned long long* keys, int64_t* ids, int n, cudaStream_t st) {
+  return rwkv_launch("argmax_finish", k_argmax_finish, dim3((n + 255) / 256), dim3(256), 0, st, keys,
+                     ids, n);
 }
 
 int launch_scatter_state_x(const __half* xlast, __half* tmix_x, __half* cmix_x, const int* slots,

@@ -166,13 +166,13 @@ class RWKV7B200(RWKV7Model):
 
     def run_batch(self, tokens: Tensor, cu: Tensor, row_seq: Tensor, slots: Tensor | None,
                   sdesc: _lib.StateDesc, logit_rows: Tensor | None, logits: Tensor | None,
-                  semantics: int) -> None:
+                  semantics: int, next_ids: Tensor | None = None) -> None:
         """One ``rwkv7_forward`` call on the current stream (all args on device)."""
         M, S = tokens.numel(), cu.numel() - 1
         n_log = 0 if logit_rows is None else logit_rows.numel()
         ws, nbytes = self._workspace(M, S, n_log)
         b = _lib.Batch(M, S, ptr(tokens), ptr(cu), ptr(row_seq), ptr(slots), n_log,
-                       ptr(logit_rows), ptr(logits), semantics)
+                       ptr(logit_rows), ptr(logits), semantics, ptr(next_ids))
         stream = torch.cuda.current_stream(self.w.device).cuda_stream
         check(self._lib.rwkv7_forward(self._cm, b, sdesc, ws, nbytes, stream))
 
@@ -258,6 +258,33 @@ class RWKV7B200(RWKV7Model):
             self.run_batch(tok[s:s + n], rows[: n + 1], rows[:n], sl, state.desc(), rows[:n],
                            logits[s:s + n], SEM_DECODE)
         return logits
+
+    def decode_batch_greedy(self, tokens: Tensor, state: BatchedState,
+                            slots: Tensor | None = None, out: Tensor | None = None) -> Tensor:
+        """One decode step of B sequences returning greedy next ids ``[B]`` int64.
+
+        Same state update as ``decode_batch``; the ids equal
+        ``decode_batch(...).argmax(-1)`` (lowest id among equal fp16 logits). On the
+        token-batch path the lm head reduces each row to its argmax inside the GEMM
+        epilogue, so the ``[B, V]`` logits are never written; the fused GEMV path
+        (B <= 4) produces logits and takes their argmax on the device.
+        """
+        tok = self._tokens(tokens)
+        B = tok.numel()
+        if slots is None and B > state.n_slots:
+            raise ValueError(f"{B} tokens but only {state.n_slots} state slots")
+        if out is None:
+            out = torch.empty(B, dtype=torch.int64, device=self.w.device)
+        if self._use_gemv(B):
+            return torch.argmax(self.decode_batch(tok, state, slots), dim=-1, out=out)
+        rows = self._arange(B + 1)
+        for s in range(0, B, self.max_rows):
+            n = min(self.max_rows, B - s)
+            sl = slots[s:s + n] if slots is not None else (
+                None if s == 0 else self._arange(B)[s:s + n])
+            self.run_batch(tok[s:s + n], rows[: n + 1], rows[:n], sl, state.desc(), rows[:n],
+                           None, SEM_DECODE, next_ids=out[s:s + n])
+        return out
 
     def prefill_batch(self, seqs: list, state: BatchedState, slots=None) -> BatchedState:
         """Prefill several sequences in one varlen batch (state only).

@@ -64,6 +64,10 @@ class ContinuousBatcher:
         self.prefill_tokens = prefill_tokens
         self.stop_token = stop_token
         self.sampling = sampling
+        t = sampling.get("temperature")
+        # greedy decoding goes through the fused greedy head when the model has one
+        self._greedy = ((t is None or t <= 0) and sampling.get("repetition_penalty", 1.0) == 1.0
+                        and hasattr(model, "decode_batch_greedy"))
         self.state = BatchedState(model.L, model.C, max_batch, device=self.dev)
         self.free = deque(range(max_batch))
         self.waiting: deque[Request] = deque()
@@ -144,8 +148,11 @@ class ContinuousBatcher:
         slots = list(self.decoding)
         sl = torch.tensor(slots, dtype=torch.int64).to(self.dev, non_blocking=True)
         tok = self.next_tok.index_select(0, sl)
-        logits = self.model.decode_batch(tok, self.state, sl.to(torch.int32))
-        nxt = sample_logits(logits, **self.sampling).to(torch.int64)
+        if self._greedy:
+            nxt = self.model.decode_batch_greedy(tok, self.state, sl.to(torch.int32))
+        else:
+            logits = self.model.decode_batch(tok, self.state, sl.to(torch.int32))
+            nxt = sample_logits(logits, **self.sampling).to(torch.int64)
         self.next_tok.index_copy_(0, sl, nxt)
         self.out.index_put_((sl, self.gen.index_select(0, sl)), nxt)
         self.gen.index_add_(0, sl, torch.ones_like(sl))

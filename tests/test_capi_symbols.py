@@ -39,7 +39,7 @@ def test_all_symbols_exported(lib):
 
 
 def test_abi_and_argument_errors_without_gpu(lib):
-    assert lib.rwkv_b200_abi_version() == 1
+    assert lib.rwkv_b200_abi_version() == 2
     assert lib.rwkv7_dplr_step(None, None, None, None, None, None, None, None, 1, 16, None) == 1
     assert b"null pointer" in lib.rwkv_b200_last_error()
     assert lib.rwkv7_gemm_f16(None, 0, 0, None) == 1

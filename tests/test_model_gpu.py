@@ -242,3 +242,53 @@ def test_small_batch_decode_paths(monkeypatch, B, mode):
     from rwkv_tl_b200 import _lib
 
     assert _lib.load().rwkv_b200_device_error() == 0
+
+
+@pytest.mark.parametrize("B", [1, 16, 200])
+def test_decode_batch_greedy_matches_argmax_of_logits(B):
+    """The greedy head (argmax inside the lm-head GEMM epilogue, no logits stored)
+    returns exactly argmax(decode_batch logits), and updates the state identically."""
+    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 3)
+    g = torch.Generator(device="cuda").manual_seed(B)
+    states = []
+    for _ in range(2):
+        bs = BatchedState(m.L, m.C, B, device="cuda")
+        states.append(bs)
+    for t in ("rnn", "tmix_x", "cmix_x"):
+        src = torch.randn(getattr(states[0], t).shape, generator=g, device="cuda")
+        src = 0.1 * src if t == "rnn" else src.half()
+        for bs in states:
+            getattr(bs, t).copy_(src)
+    toks = torch.randint(0, 4096, (B,), generator=g, device="cuda")
+    slots = torch.randperm(B, generator=g, device="cuda").to(torch.int32)
+    lg = m.decode_batch(toks, states[0], slots)
+    ids = m.decode_batch_greedy(toks, states[1], slots)
+    torch.cuda.synchronize()
+    assert ids.dtype == torch.int64 and ids.shape == (B,)
+    assert torch.equal(ids, lg.argmax(-1))
+    for t in ("rnn", "tmix_x", "cmix_x"):
+        assert torch.equal(getattr(states[0], t), getattr(states[1], t))
+
+
+def test_greedy_head_ties_pick_the_lowest_id():
+    """Rows of the head that are identical give equal fp16 logits; like torch.argmax
+    the greedy head must return the first of them."""
+    sd = synth_checkpoint(ModelConfig(n_layer=1, n_embd=768, vocab=4096), seed=4)
+    head = sd["head.weight"]
+    head[:] = 0.01 * head
+    head[100:4096:97] = 5.0 * head[7]  # ids 100, 197, 294, ... have equal, large logits
+    w = RWKV7Weight(sd, device="cuda")
+    m = RWKV7B200(w)
+    B = 32
+    bs = BatchedState(m.L, m.C, B, device="cuda")
+    toks = torch.arange(B, device="cuda")
+    lg = m.decode_batch(toks, BatchedState(m.L, m.C, B, device="cuda"))
+    ids = m.decode_batch_greedy(toks, bs)
+    torch.cuda.synchronize()
+    ref = lg.argmax(-1)
+    assert torch.equal(ids, ref)
+    # the tied rows really are tied and the winner is the lowest of them when they win
+    tied = torch.arange(100, 4096, 97, device="cuda")
+    wins = torch.isin(ref, tied)
+    assert wins.any()
+    assert torch.all(ref[wins] == 100)
