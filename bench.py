@@ -361,6 +361,17 @@ def side_measurements(model, w, dev, stream, step_bytes_of, hbm_gbs) -> dict:
             out["decode_b1_roofline"] = {"bound": "hbm", "us_per_token": ms * 1e3,
                                          "algorithmic_bytes_per_step": step_bytes_of(1),
                                          "achieved": gbs, "unit": "GB/s", "frac": gbs / hbm_gbs}
+    # B = 256 eager (no graph): logits written vs the greedy head (argmax in the GEMM epilogue)
+    eng = model.model if hasattr(model, "model") else model
+    st = BatchedState(w.L, w.C, 256, device=dev)
+    tok = torch.randint(0, w.V, (256,), device=dev)
+    for name, f in (("logits", lambda: eng.decode_batch(tok, st)),
+                    ("greedy_ids", lambda: eng.decode_batch_greedy(tok, st))):
+        for _ in range(3):
+            f()
+        ms = timed(f, 20, stream)
+        out.setdefault("decode_b256_eager", {})[name] = {"ms": ms, "tokens_per_s": 256 / (ms * 1e-3)}
+    del st
     S = State(w.L, w.C, 64, device=dev)
     toks = torch.randint(0, w.V, (4096,), device=dev)
     f = lambda: model.prefill(toks, S)  # noqa: E731
