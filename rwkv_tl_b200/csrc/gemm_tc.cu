@@ -58,6 +58,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive_plain(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)),
                "r"(bytes)
@@ -470,6 +474,237 @@ int launch_tc(const TcParams& prm, dim3 grid, cudaStream_t st) {
                      (size_t)smem_bytes<BN, STAGES>(), st, prm);
 }
 
+// ---------------------------------------------------------------------------
+// Persistent variant for large problems (every N >= 256, enough tiles to fill the
+// GPU): one CTA per SM walks 128 x 256 output tiles (M fastest, so CTAs running at
+// the same time share weight tiles in L2). An M=128 x K=16 MMA costs nearly the
+// same time at N=64, 128 or 256 (measured), so the widest tile does the most math
+// per MMA issued. Two 256-column TMEM accumulators let the epilogue warps drain
+// tile j while the MMA thread already accumulates tile j+1:
+//   tmem_full[b]  MMA -> epilogue  (tcgen05.commit after the tile's last K-block)
+//   tmem_empty[b] epilogue -> MMA  (4 arrivals, one per epilogue warp)
+// The operand ring (full/empty, PSTAGES deep) runs continuously across tiles.
+constexpr int PBN = 256, PSTAGES = 4;
+
+struct TileMap {
+  int base[4 + 1];  // first tile of each problem
+  int tiles_m[4];
+};
+
+__device__ __forceinline__ void tile_of(const TcParams& prm, const TileMap& tm, int t, int& g,
+                                        int& m0, int& n0) {
+  g = 0;
+  while (g + 1 < prm.n_problems && t >= tm.base[g + 1]) ++g;
+  const int local = t - tm.base[g];
+  m0 = (local % tm.tiles_m[g]) * BM;
+  n0 = (local / tm.tiles_m[g]) * PBN;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_gemm_tc_persist(const __grid_constant__ TcParams prm, const __grid_constant__ TileMap tm) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int A_BYTES = BM * BK * 2, B_BYTES = PBN * BK * 2;
+  unsigned char* sA = base;
+  unsigned char* sB = base + PSTAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + PSTAGES * B_BYTES);
+  uint64_t* empty = full + PSTAGES;
+  uint64_t* tfull = empty + PSTAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int total = tm.base[prm.n_problems];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(tmem_slot)),
+                 "r"(2 * PBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int it = 0;
+      bool ok = true;
+      bool waited = false;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int g, m0, n0;
+        tile_of(prm, tm, t, g, m0, n0);
+        const int nk = prm.p[g].K / BK;
+        // the first tile's weight stages go out before the programmatic wait
+        int pre = 0;
+        if (!waited) {
+          pre = min(PSTAGES, nk);
+          for (int i = 0; i < pre; ++i) {
+            mbar_expect_tx(&full[i], A_BYTES + B_BYTES);
+            tma_load_2d(sB + i * B_BYTES, &prm.tb[g], &full[i], i * BK, n0);
+          }
+          grid_dep_wait();
+          grid_dep_trigger();
+          waited = true;
+          for (int i = 0; i < pre; ++i) tma_load_2d(sA + i * A_BYTES, &prm.ta[g], &full[i], i * BK, m0);
+          it = pre;
+        }
+        for (int kb = pre; kb < nk; ++kb, ++it) {
+          const int s = it % PSTAGES;
+          const uint32_t r = it / PSTAGES;
+          if (r > 0 && !mbar_wait(&empty[s], (r & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &prm.ta[g], &full[s], kb * BK, m0);
+          tma_load_2d(sB + s * B_BYTES, &prm.tb[g], &full[s], kb * BK, n0);
+        }
+      }
+      if (!waited) {
+        grid_dep_wait();
+        grid_dep_trigger();
+      }
+      // drain: never leave the CTA while copies may still land in shared memory
+      for (int i = max(0, it - PSTAGES); i < it; ++i) mbar_wait(&full[i % PSTAGES], (i / PSTAGES) & 1);
+    } else {
+      grid_dep_wait();
+      grid_dep_trigger();
+    }
+  } else if (warp == 1) {
+    grid_dep_wait();
+    grid_dep_trigger();
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = instr_desc<PBN>();
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++j) {
+        int g, m0, n0;
+        tile_of(prm, tm, t, g, m0, n0);
+        const int nk = prm.p[g].K / BK;
+        const int b = j & 1;
+        const uint32_t u = (uint32_t)(j >> 1);
+        // accumulator b must have been drained by the epilogue of its previous tile
+        if (u > 0 && !mbar_wait(&tempty[b], (u & 1) ^ 1)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + (uint32_t)(b * PBN);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % PSTAGES;
+          if (!mbar_wait(&full[s], (it / PSTAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t ad = smem_desc_sw128(sA + s * A_BYTES);
+          const uint64_t bd = smem_desc_sw128(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), idesc,
+                     (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tfull[b]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5), overlapped with the next tile's MMAs ----------------
+    grid_dep_wait();
+    grid_dep_trigger();
+    const int quad = warp & 3;
+    int j = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++j) {
+      const int b = j & 1;
+      const bool ok = mbar_wait(&tfull[b], (uint32_t)(j >> 1) & 1);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (!__all_sync(0xffffffffu, ok)) break;
+      int g, m0, n0;
+      tile_of(prm, tm, t, g, m0, n0);
+      const TcProblem& P = prm.p[g];
+      const int row = m0 + quad * 32 + lane;
+      const uint32_t trow = tmem + (uint32_t)(b * PBN) + ((uint32_t)(quad * 32) << 16);
+      void* C = P.C;
+      const __half* R = static_cast<const __half*>(P.R);
+      if constexpr (EPI == EPI_ARGMAX) {
+        unsigned long long best = 0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < PBN; c0 += 16) {
+          float v[16];
+          tmem_ld16(trow + c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int col = n0 + c0 + i;
+            if (col < P.N) {
+              const unsigned long long key = argmax_key(r16(v[i]), col);
+              best = key > best ? key : best;
+            }
+          }
+        }
+        if (row < P.M) atomicMax(static_cast<unsigned long long*>(C) + row, best);
+      } else {
+        const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < PBN; c0 += 16) {
+          float v[16];
+          tmem_ld16(trow + c0, v);
+          const int col = n0 + c0;
+          if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec, g);
+        }
+      }
+      // accumulator b is free again
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_plain(&tempty[b]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * PBN));
+  }
+}
+
+constexpr int persist_smem_bytes() {
+  return 1024 + PSTAGES * (BM * BK * 2 + PBN * BK * 2) + (2 * PSTAGES + 4) * 8 + 16;
+}
+
+template <int EPI>
+int launch_tc_persist(const TcParams& prm, const TileMap& tm, cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool done[64] = {};
+  static int n_sm[64] = {};
+  if (dev < 64 && !done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc_persist<EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         persist_smem_bytes());
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) {
+      rwkv_set_error("gemm_tc_persist: setup: %s", cudaGetErrorString(e));
+      return RWKV_ERR_CUDA;
+    }
+    done[dev] = true;
+  }
+  const int total = tm.base[prm.n_problems];
+  const int grid = min(total, dev < 64 ? n_sm[dev] : 148);
+  return rwkv_launch("gemm_tc_persist", k_gemm_tc_persist<EPI>, dim3(grid), dim3(NTHREADS),
+                     (size_t)persist_smem_bytes(), st, prm, tm);
+}
+
 }  // namespace
 
 // True when every problem fits the tcgen05 path (K multiple of 64, aligned operands).
@@ -486,6 +721,48 @@ bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n) {
 template <int BN, int STAGES>
 int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
                        bool defer, cudaStream_t st);
+
+// RWKV_B200_GEMM_PERSIST=0 turns the persistent large-problem kernel off.
+bool gemm_persist_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("RWKV_B200_GEMM_PERSIST");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Persistent 128 x 256 tiles over every problem of the group (splits = 1).
+int gemm_tc_launch_persist(const rwkv7_gemm_problem* p, int n, int epi, cudaStream_t st) {
+  TcParams prm;
+  TileMap tm;
+  memset(&prm, 0, sizeof(prm));
+  memset(&tm, 0, sizeof(tm));
+  prm.n_problems = n;
+  prm.splits = 1;
+  for (int i = 0; i < n; ++i) {
+    int rc = make_map(&prm.ta[i], p[i].A, p[i].M, p[i].K, p[i].lda, BM);
+    if (rc) return rc;
+    rc = make_map(&prm.tb[i], p[i].B, p[i].N, p[i].K, p[i].ldb, PBN);
+    if (rc) return rc;
+    prm.p[i].C = p[i].C;
+    prm.p[i].R = p[i].R;
+    prm.p[i].M = p[i].M;
+    prm.p[i].N = p[i].N;
+    prm.p[i].K = p[i].K;
+    prm.p[i].ldc = p[i].ldc;
+    tm.tiles_m[i] = (p[i].M + BM - 1) / BM;
+    tm.base[i + 1] = tm.base[i] + tm.tiles_m[i] * ((p[i].N + PBN - 1) / PBN);
+  }
+  switch (epi) {
+    case RWKV_EPI_STORE: return launch_tc_persist<RWKV_EPI_STORE>(prm, tm, st);
+    case RWKV_EPI_RESID: return launch_tc_persist<RWKV_EPI_RESID>(prm, tm, st);
+    case RWKV_EPI_RELUSQ: return launch_tc_persist<RWKV_EPI_RELUSQ>(prm, tm, st);
+    case RWKV_EPI_STORE_F32: return launch_tc_persist<RWKV_EPI_STORE_F32>(prm, tm, st);
+    case EPI_ARGMAX: return launch_tc_persist<EPI_ARGMAX>(prm, tm, st);
+  }
+  rwkv_set_error("gemm_tc_persist: epilogue %d not supported", epi);
+  return RWKV_ERR_ARG;
+}
 
 // Tile configuration and split-K by problem size. Large grids: 128 x 128 tiles,
 // 3 stages (two CTAs per SM). Small grids (batched decode): 128 x 64 tiles with 6
@@ -508,7 +785,12 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_
     n4 = n4 && p[i].N % 4 == 0 && p[i].ldc % 2 == 0;
   }
   if (splits_out) *splits_out = 1;
-  if (tiles128 >= 148) return gemm_tc_launch_cfg<128, 3>(p, n, epi, 1, ws, false, st);
+  if (tiles128 >= 148) {
+    bool wide = epi != RWKV_EPI_LORA_ACT && epi != RWKV_EPI_LORA_ACT2;
+    for (int i = 0; i < n; ++i) wide = wide && p[i].N >= PBN;
+    if (wide && gemm_persist_enabled()) return gemm_tc_launch_persist(p, n, epi, st);
+    return gemm_tc_launch_cfg<128, 3>(p, n, epi, 1, ws, false, st);
+  }
   int splits = 1;
   if (ws && n4 && tiles64 < 48 && epi != EPI_ARGMAX) {
     splits = max(1, min(min_kb / 8, (128 + tiles64 - 1) / tiles64));

@@ -69,3 +69,30 @@ def test_gemm_grouped_epilogues():
     assert (C.float() - (R.float() + acc)).abs().max() < 1e-2
     _run([(A, B, C, None)], 2)
     assert (C.float() - torch.relu(acc) ** 2).abs().max() < 2e-2 * (acc.abs().max() ** 2)
+
+
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_gemm_large_grouped_ragged_epilogues(epi, gemm_kernel):
+    """Large grouped problems (the persistent 128 x 256-tile kernel on the tcgen05 path):
+    ragged M and N edges, every epilogue, two problems of different N in one launch."""
+    g = torch.Generator(device="cuda").manual_seed(40 + epi)
+    M, K = 1000, 1024
+    A = [torch.randn(M, K, device="cuda", generator=g).half() for _ in range(2)]
+    B = [(torch.randn(n, K, device="cuda", generator=g) / 32).half() for n in (1280, 1100)]
+    R = [torch.randn(M, n, device="cuda", generator=g).half() if epi == 1 else None
+         for n in (1280, 1100)]
+    dt = torch.float32 if epi == 3 else torch.float16
+    C = [torch.full((M, n), 7.0, device="cuda", dtype=dt) for n in (1280, 1100)]
+    _run([(A[i], B[i], C[i], R[i]) for i in range(2)], epi)
+    for i in range(2):
+        acc = A[i].float() @ B[i].float().t()
+        if epi == 0:
+            ref = acc.half().float()
+        elif epi == 1:
+            ref = (R[i].float() + acc.half().float()).half().float()
+        elif epi == 2:
+            ref = (torch.relu(acc.half().float()) ** 2).half().float()
+        else:
+            ref = acc
+        err = (C[i].float() - ref).abs().max()
+        assert err <= 2e-3 * ref.abs().max() + 1e-3, (i, float(err))

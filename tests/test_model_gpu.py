@@ -244,11 +244,12 @@ def test_small_batch_decode_paths(monkeypatch, B, mode):
     assert _lib.load().rwkv_b200_device_error() == 0
 
 
-@pytest.mark.parametrize("B", [1, 16, 200])
-def test_decode_batch_greedy_matches_argmax_of_logits(B):
+@pytest.mark.parametrize("B,V", [(1, 4096), (16, 4096), (200, 4096), (200, 65536)])
+def test_decode_batch_greedy_matches_argmax_of_logits(B, V):
     """The greedy head (argmax inside the lm-head GEMM epilogue, no logits stored)
-    returns exactly argmax(decode_batch logits), and updates the state identically."""
-    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 3)
+    returns exactly argmax(decode_batch logits), and updates the state identically.
+    V = 65536 puts the head on the persistent 128 x 256-tile GEMM."""
+    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=V), 3)
     g = torch.Generator(device="cuda").manual_seed(B)
     states = []
     for _ in range(2):
@@ -259,12 +260,24 @@ def test_decode_batch_greedy_matches_argmax_of_logits(B):
         src = 0.1 * src if t == "rnn" else src.half()
         for bs in states:
             getattr(bs, t).copy_(src)
-    toks = torch.randint(0, 4096, (B,), generator=g, device="cuda")
+    toks = torch.randint(0, V, (B,), generator=g, device="cuda")
     slots = torch.randperm(B, generator=g, device="cuda").to(torch.int32)
     lg = m.decode_batch(toks, states[0], slots)
     ids = m.decode_batch_greedy(toks, states[1], slots)
     torch.cuda.synchronize()
     assert ids.dtype == torch.int64 and ids.shape == (B,)
+    if m._use_gemv(B):
+        # the fused small-batch kernel sums residuals with float atomics: two runs from the
+        # same state may differ in the last bit, so near-ties may flip; the chosen logit
+        # must still be the row maximum to within that noise
+        best = lg.float().max(-1).values
+        picked = lg.float().gather(1, ids[:, None])[:, 0]
+        assert torch.all(picked >= best - 2e-3 * best.abs().clamp(min=1.0))
+        for t in ("rnn", "tmix_x", "cmix_x"):
+            a, b = getattr(states[0], t).float(), getattr(states[1], t).float()
+            assert (a - b).norm() <= 1e-3 * a.norm()
+        return
+    # token-batch path: deterministic (split-K slices summed in order), so exact
     assert torch.equal(ids, lg.argmax(-1))
     for t in ("rnn", "tmix_x", "cmix_x"):
         assert torch.equal(getattr(states[0], t), getattr(states[1], t))
