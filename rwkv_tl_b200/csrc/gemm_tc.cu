@@ -656,13 +656,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (row < P.M) atomicMax(static_cast<unsigned long long*>(C) + row, best);
       } else {
-        const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
+        const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(R) & 15) == 0;
+        if (EPI == RWKV_EPI_RESID && vec && n0 + PBN <= P.N) {
+          // residual rows: fetch the thread's whole 128-column slice first, so the tile
+          // pays one memory latency per half instead of one per 16 columns
 #pragma unroll 1
-        for (int c0 = 0; c0 < PBN; c0 += 16) {
-          float v[16];
-          tmem_ld16(trow + c0, v);
-          const int col = n0 + c0;
-          if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec, g);
+          for (int h0 = 0; h0 < PBN; h0 += 128) {
+            uint4 rr[16];
+            const __half* rp = R + (size_t)row * P.ldc + n0 + h0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              rr[i] = row < P.M ? *reinterpret_cast<const uint4*>(rp + 8 * i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int c1 = 0; c1 < 128; c1 += 16) {
+              float v[16];
+              tmem_ld16(trow + h0 + c1, v);
+              if (row < P.M) {
+                uint4 pk[2];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  const __half2* r2 = reinterpret_cast<const __half2*>(&rr[c1 / 8 + q]);
+                  __half2* o2 = reinterpret_cast<__half2*>(&pk[q]);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float2 rf = __half22float2(r2[e]);
+                    o2[e] = __floats2half2_rn(rf.x + r16(v[8 * q + 2 * e]), rf.y + r16(v[8 * q + 2 * e + 1]));
+                  }
+                }
+                __half* cp = static_cast<__half*>(C) + (size_t)row * P.ldc + n0 + h0 + c1;
+                reinterpret_cast<uint4*>(cp)[0] = pk[0];
+                reinterpret_cast<uint4*>(cp)[1] = pk[1];
+              }
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c0 = 0; c0 < PBN; c0 += 16) {
+            float v[16];
+            tmem_ld16(trow + c0, v);
+            const int col = n0 + c0;
+            if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec, g);
+          }
         }
       }
       // accumulator b is free again
