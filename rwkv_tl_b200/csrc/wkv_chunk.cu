@@ -65,7 +65,7 @@ __global__ void k_chunk_table(const int* __restrict__ cu, int* __restrict__ chun
 
 // grid = (max_chunks, H), block = 256. Rows past the sequence end are padded
 // with identity transitions (w = 1, a = b = k = r = 0).
-__global__ void __launch_bounds__(256) k_chunk_prep(
+__global__ void __launch_bounds__(256, 4) k_chunk_prep(
     const __half* __restrict__ rb, const __half* __restrict__ wb, const __half* __restrict__ kb,
     const __half* __restrict__ vb, const __half* __restrict__ ab, const __half* __restrict__ bb,
     const int* __restrict__ cu,
@@ -75,6 +75,7 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
   __shared__ float Aab[CL][CL + 1], Aak[CL][CL + 1], Brb[CL][CL + 1], Brk[CL][CL + 1],
       Tm[CL][CL + 1], PU[CL][CL + 1], PY[CL][CL + 1];
   __shared__ float sv_[CL * RS];
+  __shared__ float glv[KD];  // e^{G_L}: the chunk's total decay per key column
   __shared__ float Wh[CL * RS];
   __shared__ int info[3];
   const int c = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
@@ -100,17 +101,22 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
   if (!info[0]) return;
   const int m0 = info[1], n = info[2];
   const int hc = h * KD;
-  // 1. load (fp16 -> fp32), pad
-  for (int i = tid; i < CL * KD; i += 256) {
-    const int t = i / KD, k = i % KD;
-    float r = 0.f, w = 1.f, kk = 0.f, vv = 0.f, a = 0.f, b = 0.f;
+  // 1. load (fp16 -> fp32, two channels per thread), pad
+  for (int i = tid; i < CL * KD / 2; i += 256) {
+    const int t = i / (KD / 2), k = 2 * (i % (KD / 2));
+    float2 r = make_float2(0.f, 0.f), w = make_float2(1.f, 1.f), kk = r, vv = r, a = r, b = r;
     if (t < n) {
       const size_t o = (size_t)(m0 + t) * C + hc + k;
-      r = h2f(rb[o]); w = h2f(wb[o]); kk = h2f(kb[o]); vv = h2f(vb[o]); a = h2f(ab[o]); b = h2f(bb[o]);
+      auto ld = [&](const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p + o)); };
+      r = ld(rb); w = ld(wb); kk = ld(kb); vv = ld(vb); a = ld(ab); b = ld(bb);
     }
-    sv_[t * RS + k] = vv;
-    sr_[t * RS + k] = r; sg[t * RS + k] = logf(w); sk_[t * RS + k] = kk; sa_[t * RS + k] = a;
-    sb_[t * RS + k] = b;
+    const int q = t * RS + k;
+    sv_[q] = vv.x; sv_[q + 1] = vv.y;
+    sr_[q] = r.x; sr_[q + 1] = r.y;
+    sg[q] = logf(w.x); sg[q + 1] = logf(w.y);
+    sk_[q] = kk.x; sk_[q + 1] = kk.y;
+    sa_[q] = a.x; sa_[q + 1] = a.y;
+    sb_[q] = b.x; sb_[q + 1] = b.y;
   }
   __syncthreads();
   // 2. cumulative log decay per column, then decay-scaled vectors
@@ -126,6 +132,7 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
       sr_[t * RS + tid] *= eg;
       sg[t * RS + tid] = g;
     }
+    glv[tid] = expf(g);
   }
   __syncthreads();
   // 3. the four L x L interaction matrices
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
     float v = sr_[t * RS + k];
     for (int q = 0; q <= t; ++q) v += Brb[t][q] * Wh[q * RS + k];
     out[OFF_Q + t * KD + k] = v;
-    const float gl = expf(sg[(CL - 1) * RS + k]);
+    const float gl = glv[k];
     out[OFF_B + t * KD + k] = sb_[t * RS + k] * gl;
     if (t == 0) out[OFF_G + k] = gl;
   }
@@ -193,26 +200,49 @@ __global__ void __launch_bounds__(256) k_chunk_prep(
     PY[t][j] = v;
   }
   __syncthreads();
-  // 7. the value-dependent terms per state row: (PU v)_t, (PY v)_t and U = sum_j v_j Kt_j
-  for (int i = tid; i < KD * CL; i += 256) {
-    const int row = i / CL, t = i % CL;
-    float pu = 0.f, py = 0.f;
-#pragma unroll
+  // 7. the value-dependent terms per state row: (PU v)_t, (PY v)_t and U = sum_j v_j Kt_j,
+  // register-blocked over 4 state rows per thread
+  {
+    const int t = tid & 15, r0 = (tid >> 4) * 4;
+    float pu[4] = {}, py[4] = {};
+#pragma unroll 4
     for (int j = 0; j < CL; ++j) {
-      const float vj = sv_[j * RS + row];
-      pu += PU[t][j] * vj;
-      py += PY[t][j] * vj;
-    }
-    float* o = out + OFF_RW + row * RWS;
-    o[t] = pu;
-    o[CL + t] = py;
-  }
-  for (int i = tid; i < KD * KD; i += 256) {
-    const int row = i / KD, k = i % KD;
-    float u = 0.f;
+      const float a = PU[t][j], b = PY[t][j];
 #pragma unroll
-    for (int j = 0; j < CL; ++j) u += sv_[j * RS + row] * sk_[j * RS + k];
-    out[OFF_RW + row * RWS + 2 * CL + k] = u * expf(sg[(CL - 1) * RS + k]);
+      for (int r = 0; r < 4; ++r) {
+        const float vj = sv_[j * RS + r0 + r];
+        pu[r] += a * vj;
+        py[r] += b * vj;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float* o = out + OFF_RW + (r0 + r) * RWS;
+      o[t] = pu[r];
+      o[CL + t] = py[r];
+    }
+  }
+  {
+    const int k0 = (tid & 15) * 4, r0 = (tid >> 4) * 4;
+    float u[4][4] = {};
+#pragma unroll 2
+    for (int j = 0; j < CL; ++j) {
+      float vv[4], kk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        vv[e] = sv_[j * RS + r0 + e];
+        kk[e] = sk_[j * RS + k0 + e];
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) u[r][c] += vv[r] * kk[c];
+    }
+    const float4 g4 = make_float4(glv[k0], glv[k0 + 1], glv[k0 + 2], glv[k0 + 3]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      *reinterpret_cast<float4*>(out + OFF_RW + (r0 + r) * RWS + 2 * CL + k0) =
+          make_float4(u[r][0] * g4.x, u[r][1] * g4.y, u[r][2] * g4.z, u[r][3] * g4.w);
   }
 }
 
