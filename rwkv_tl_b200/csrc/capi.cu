@@ -57,7 +57,8 @@ bool rwkv_chain_take_pdl() {
 int decode_persist_timeout_flag();
 int wkv_chunk_bad_flag();
 extern "C" int rwkv_b200_device_error(void) {
-  const int a = gemm_tc_timeout_flag(), b = decode_persist_timeout_flag(), c = wkv_chunk_bad_flag();
+  const int a = gemm_tc_timeout_flag() != 0, b = decode_persist_timeout_flag() != 0,
+            c = wkv_chunk_bad_flag() != 0;
   return a | (b << 1) | (c << 2);
 }
 
