@@ -481,9 +481,11 @@ def main():
                     help="run only config 4 (continuous batching of N_SEQS requests, 128 new "
                          "tokens each, sharded over the ranks) and print its JSON line")
     args = ap.parse_args()
-    world, rank, local = dist_setup() if args.impl == "b200" or int(
-        os.environ.get("WORLD_SIZE", "1")) == 1 else (int(os.environ["WORLD_SIZE"]),
-                                                      int(os.environ.get("RANK", "0")), 0)
+    if args.impl == "b200":
+        world, rank, local = dist_setup()
+    else:  # the reference arm is CPU-only: rank 0 runs it, the other ranks exit
+        world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")),
+                              int(os.environ.get("RANK", "0")), 0)
     if args.profile:
         run_profile(args)
     elif args.continuous and args.impl == "b200":
