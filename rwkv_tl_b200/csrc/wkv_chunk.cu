@@ -493,13 +493,19 @@ size_t wkv_chunk_record_bytes(int M, int S, int H) {
 
 // Chunked recurrence only: y (fp16) for every row, state updated in place.
 // r..b, y: [M, C] rows (C = H * 64); rnn: [slots, H, 64, 64].
+// chunk_cu[s] = chunks before sequence s; depends on the sequence table only, so a
+// forward computes it once for all layers.
+int launch_chunk_table(const int* cu, int* chunk_cu, int S, cudaStream_t st) {
+  return rwkv_launch("chunk_table", k_chunk_table, dim3(1), dim3(1024), 0, st, cu, chunk_cu, S);
+}
+
+// Chunk transforms + scan of one layer; `chunk_cu` must already hold the chunk table.
 int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
                        const __half* a, const __half* b, float* rnn, const int* cu,
                        const int* slots, __half* ybuf, float* rec, int* chunk_cu, int M, int S,
                        int H, int n_slots, cudaStream_t st) {
   const int C = H * KD;
-  int rc = rwkv_launch("chunk_table", k_chunk_table, dim3(1), dim3(1024), 0, st, cu, chunk_cu, S);
-  if (rc) return rc;
+  int rc;
   if ((rc = rwkv_launch("chunk_prep", k_chunk_prep, dim3(M / CL + S, H), dim3(256), 0, st, r, w, k,
                         v, a, b, cu, chunk_cu, S, C, M, rec)))
     return rc;
@@ -580,6 +586,7 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
   int rc = rwkv_launch("uniform_cu", k_uniform_cu, dim3((n_seq + 256) / 256), dim3(256), 0, st, cu,
                        n_seq, T);
   if (rc) return rc;
+  if ((rc = launch_chunk_table(cu, chunk_cu, n_seq, st))) return rc;
   return launch_wkv_chunked((const __half*)r, (const __half*)w, (const __half*)k,
                             (const __half*)v, (const __half*)a, (const __half*)b, (float*)S, cu,
                             nullptr, (__half*)y, rec, chunk_cu, n_seq * T, n_seq, H, n_seq, st);
