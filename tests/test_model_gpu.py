@@ -192,7 +192,7 @@ def test_errors():
         make_rwkv7(torch.device("cuda"), backend="nope")
 
 
-@pytest.mark.parametrize("lens", [[70], [1, 33, 16, 100], [17, 5]])
+@pytest.mark.parametrize("lens", [[70], [1, 33, 16, 100], [17, 5], [300, 700, 17, 257]])
 def test_chunked_wkv_matches_serial(monkeypatch, lens):
     """The chunk-parallel wkv and the per-token wkv give the same model state (to the
     fp32 noise that fp16 rounding amplifies through the layers: state rel 1e-3)."""
