@@ -91,7 +91,8 @@ int launch_wkv_tokens(int sem, const __half* rbuf, const __half* gbuf, size_t pl
 int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
                    size_t ws_floats, cudaStream_t st, int* splits_out = nullptr);
 size_t wkv_chunk_record_bytes(int M, int S, int H);
-int launch_chunk_table(const int* cu, int* chunk_cu, int S, cudaStream_t st);
+int launch_chunk_table(const int* cu, int* chunk_cu, float* rec, int M, int S, int H,
+                       cudaStream_t st);
 int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
                        const __half* a, const __half* b, float* rnn, const int* cu,
                        const int* slots, __half* ybuf, float* rec, int* chunk_cu, int M, int S,
@@ -253,7 +254,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   auto defer = [&](int splits, const __half* res) {
     pend = splits > 1 ? PendingResid{w.splitk, res, splits} : PendingResid{nullptr, nullptr, 0};
   };
-  if (chunked) TRY(launch_chunk_table(b->cu_seqlens, w.chunk_cu, S, st));
+  if (chunked) TRY(launch_chunk_table(b->cu_seqlens, w.chunk_cu, w.chunk_rec, M, S, H, st));
   for (int l = 0; l < L; ++l) {
     const rwkv7_layer& Lw = model->layers[l];
     const __half* wrkv = (const __half*)Lw.w_rkv;

@@ -34,33 +34,61 @@ constexpr int REC = SHARED_F + KD * RWS;      // floats per (chunk, head) record
 constexpr int OFF_W = 0, OFF_Q = CL * KD, OFF_B = 2 * CL * KD, OFF_G = 3 * CL * KD,
               OFF_RW = SHARED_F;
 constexpr int RS = KD + 1;  // padded smem row stride (conflict-free column walks)
+// Two-level scan: a sequence's chunks are cut into segments of SEG chunks (256 tokens).
+// Segments are scanned concurrently (the first from the true state, the others from
+// zero); each segment's transfer matrix Phi (product of its chunk maps) then carries
+// the true state across segments, and Q Phi corrects the later segments' outputs.
+constexpr int SEG = 16;
 }  // namespace
 
-// chunk_cu[s] = number of chunks before sequence s (single block, S <= 65536).
-__global__ void k_chunk_table(const int* __restrict__ cu, int* __restrict__ chunk_cu, int S) {
+// chunk_cu[s] = chunks before sequence s, seg_cu[s] = segments (SEG chunks each) before
+// sequence s (single block, S <= 65536).
+__global__ void k_chunk_table(const int* __restrict__ cu, int* __restrict__ chunk_cu,
+                              int* __restrict__ seg_cu, int S) {
   RWKV_GRID_DEP_ENTRY();
-  __shared__ int part[1024];
+  __shared__ int part[2][1024];
   const int tid = threadIdx.x;
   const int per = (S + blockDim.x - 1) / blockDim.x;
-  int local = 0;
-  for (int i = tid * per; i < min(S, (tid + 1) * per); ++i) local += (cu[i + 1] - cu[i] + CL - 1) / CL;
-  part[tid] = local;
+  int lc = 0, ls = 0;
+  for (int i = tid * per; i < min(S, (tid + 1) * per); ++i) {
+    const int n = (cu[i + 1] - cu[i] + CL - 1) / CL;
+    lc += n;
+    ls += (n + SEG - 1) / SEG;
+  }
+  part[0][tid] = lc;
+  part[1][tid] = ls;
   __syncthreads();
-  if (tid == 0) {
+  if (tid < 2) {
     int run = 0;
     for (int i = 0; i < (int)blockDim.x; ++i) {
-      const int x = part[i];
-      part[i] = run;
+      const int x = part[tid][i];
+      part[tid][i] = run;
       run += x;
     }
   }
   __syncthreads();
-  int run = part[tid];
+  int rc = part[0][tid], rs = part[1][tid];
   for (int i = tid * per; i < min(S, (tid + 1) * per); ++i) {
-    chunk_cu[i] = run;
-    run += (cu[i + 1] - cu[i] + CL - 1) / CL;
+    chunk_cu[i] = rc;
+    seg_cu[i] = rs;
+    const int n = (cu[i + 1] - cu[i] + CL - 1) / CL;
+    rc += n;
+    rs += (n + SEG - 1) / SEG;
   }
-  if (tid == (int)blockDim.x - 1) chunk_cu[S] = run;
+  if (tid == (int)blockDim.x - 1) {
+    chunk_cu[S] = rc;
+    seg_cu[S] = rs;
+  }
+}
+
+// Largest s in [0, S) with tab[s] <= x (tab non-decreasing, tab[0] = 0).
+__device__ __forceinline__ int seq_of(const int* tab, int S, int x) {
+  int lo = 0, hi = S - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tab[mid] <= x) lo = mid; else hi = mid - 1;
+  }
+  return lo;
 }
 
 // grid = (max_chunks, H), block = 256. Rows past the sequence end are padded
@@ -306,21 +334,22 @@ __device__ __forceinline__ float dot4(float4 a, float2 s01, float2 s23) {
   return p.x + p.y;
 }
 
-constexpr int SCAN_ROWS = 8;                        // state rows per CTA
-constexpr int SCAN_THREADS = 128;                   // four warps, two rows each
+constexpr int SCAN_ROWS = 16;                       // state rows per CTA
+constexpr int SCAN_THREADS = 256;                   // eight warps, two rows each
 constexpr int SLICE_F = SCAN_ROWS * RWS;            // per-CTA part of a record's row terms
 constexpr int STAGE_F = SHARED_F + SLICE_F;         // floats per ring stage
-// Chunk records in flight per CTA. Eight stages (125 KB) also keep a second scan CTA
-// off the SM: placed early by programmatic dependent launch, CTAs could otherwise
-// pile up two or three per SM, and the slowest SM sets the scan's time.
-constexpr int NSTAGE = 8;
+// Chunk records in flight per CTA: a segment has at most SEG chunks and several
+// segment CTAs share an SM, so a short ring (47 KB, four CTAs per SM) suffices.
+constexpr int NSTAGE = 3;
 constexpr size_t SCAN_SMEM = (size_t)NSTAGE * STAGE_F * sizeof(float) + 2 * NSTAGE * sizeof(uint64_t);
 static_assert((SHARED_F * 4) % 16 == 0 && (SLICE_F * 4) % 16 == 0 && (REC * 4) % 16 == 0,
               "bulk copies need 16-byte multiples");
-static_assert(SCAN_SMEM > 114 * 1024 && SCAN_SMEM <= 227 * 1024, "one scan CTA per SM");
 }  // namespace
 
-// grid = (S, H, KD / 8 row groups), block = 128. Each half-warp owns one state row
+// grid = (max segments, H, KD / 8 row groups), block = 128: one segment of one
+// sequence per CTA (segment 0 starts from the sequence's state in rnn and writes final
+// fp16 outputs; later segments start from zero and write fp32 outputs to yf32 and
+// their end state to lbuf, for k_seg_combine / k_seg_fix). Each half-warp owns one state row
 // (lane l of the half holds keys 4l..4l+3 of it), so a warp carries two rows. Chunk
 // records stream through an NSTAGE ring of 1-D bulk copies (mbarrier full / empty).
 // Per chunk a half-warp forms the 16 What and 16 Q dot products of its row, reduces
@@ -331,24 +360,32 @@ static_assert(SCAN_SMEM > 114 * 1024 && SCAN_SMEM <= 227 * 1024, "one scan CTA p
 //   s <- s * gL + sum_j sa_j Bt_j + U.
 __global__ void __launch_bounds__(SCAN_THREADS) k_chunk_scan(
     const float* __restrict__ rec, const int* __restrict__ cu, const int* __restrict__ chunk_cu,
-    const int* __restrict__ slots, float* __restrict__ rnn, __half* __restrict__ ybuf, int C,
+    const int* __restrict__ seg_cu, const int* __restrict__ slots, float* __restrict__ rnn,
+    __half* __restrict__ ybuf, float* __restrict__ yf32, float* __restrict__ lbuf, int S, int C,
     int M, int max_chunks, int n_slots) {
   RWKV_GRID_DEP_ENTRY();
   extern __shared__ __align__(128) float scan_smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(scan_smem + (size_t)NSTAGE * STAGE_F);
   uint64_t* empty = full + NSTAGE;
-  const int s = blockIdx.x, h = blockIdx.y, H = gridDim.y, grp = blockIdx.z;
+  const int gs = blockIdx.x, h = blockIdx.y, H = gridDim.y, grp = blockIdx.z;
+  if (gs >= seg_cu[S]) return;
+  const int s = seq_of(seg_cu, S, gs);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hl = lane & 15, lrow = warp * 2 + (lane >> 4);
   const int row = grp * SCAN_ROWS + lrow;
   const int slot = slots ? slots[s] : s;
-  const int c0 = chunk_cu[s], c1 = chunk_cu[s + 1];
-  const int m_beg = cu[s], m_end = cu[s + 1];
-  if (slot < 0 || slot >= n_slots || c0 < 0 || c1 < c0 || c1 > max_chunks || m_beg < 0 ||
-      m_end < m_beg || m_end > M || (m_end - m_beg + CL - 1) / CL != c1 - c0) {
+  const int cs = chunk_cu[s], ce = chunk_cu[s + 1];
+  const int nseg = seg_cu[s + 1] - seg_cu[s], g = gs - seg_cu[s];
+  const int m_seq = cu[s], m_end = cu[s + 1];
+  if (slot < 0 || slot >= n_slots || cs < 0 || ce < cs || ce > max_chunks || m_seq < 0 ||
+      m_end < m_seq || m_end > M || (m_end - m_seq + CL - 1) / CL != ce - cs ||
+      nseg != (ce - cs + SEG - 1) / SEG) {
     if (tid == 0) atomicOr(&g_chunk_bad, 1);
     return;
   }
+  // this CTA's segment: chunks [c0, c1), tokens from m_beg
+  const int c0 = cs + g * SEG, c1 = min(ce, c0 + SEG);
+  const int m_beg = m_seq + g * SEG * CL;
   if (tid == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
       sc_mbar_init(&full[i], 1);
@@ -358,7 +395,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) k_chunk_scan(
   }
   __syncthreads();
   float* Srow = rnn + (((size_t)slot * H + h) * KD + row) * KD + 4 * hl;
-  float4 st = *reinterpret_cast<const float4*>(Srow);
+  float4 st = g == 0 ? *reinterpret_cast<const float4*>(Srow) : make_float4(0.f, 0.f, 0.f, 0.f);
   int issued = 0;  // chunks whose copies thread 0 has issued
   auto issue = [&](int c) {
     const int buf = (c - c0) % NSTAGE;
@@ -406,9 +443,15 @@ __global__ void __launch_bounds__(SCAN_THREADS) k_chunk_scan(
     const float o0 = p[0] + add.x, o1 = p[1] + add.y;
     if (hl >= 8) {
       const int m0 = m_beg + it * CL + 2 * hl - CL;
-      __half* yp = ybuf + (size_t)m0 * C + h * KD + row;
-      if (m0 < m_end) yp[0] = f2h(o0);
-      if (m0 + 1 < m_end) yp[C] = f2h(o1);
+      if (g == 0) {  // final outputs
+        __half* yp = ybuf + (size_t)m0 * C + h * KD + row;
+        if (m0 < m_end) yp[0] = f2h(o0);
+        if (m0 + 1 < m_end) yp[C] = f2h(o1);
+      } else {  // partial outputs: k_seg_fix adds the incoming state's part
+        float* yp = yf32 + (size_t)m0 * C + h * KD + row;
+        if (m0 < m_end) yp[0] = o0;
+        if (m0 + 1 < m_end) yp[C] = o1;
+      }
     }
     const float4 gl = *reinterpret_cast<const float4*>(R + OFF_G + 4 * hl);
     const float4 u = *reinterpret_cast<const float4*>(RW + 2 * CL + 4 * hl);
@@ -446,7 +489,282 @@ __global__ void __launch_bounds__(SCAN_THREADS) k_chunk_scan(
       }
     return;
   }
-  *reinterpret_cast<float4*>(Srow) = st;
+  if (nseg == 1)
+    *reinterpret_cast<float4*>(Srow) = st;
+  else
+    *reinterpret_cast<float4*>(lbuf + (((size_t)gs * H + h) * KD + row) * KD + 4 * hl) = st;
+}
+
+// ---- two-level scan: segment transfers, the cross-segment pass, output correction ----
+//
+// Chunk map of one state row s (a vector over keys), from the chunk record:
+//   s' = A s + u,  A = diag(gL) + Bt^T What   (u: the value terms, independent of s)
+// so a segment's true start state S_g (64 rows) reaches chunk c as Phi_c S_g + (the
+// zero-start scan), Phi_c = A_{c-1} ... A_{first}, and the chunk's outputs gain
+// (Q_c Phi_c) S_g. All fp32.
+
+// 3xTF32 tensor-core products (mma.sync m16n8k8 .tf32, fp32 accumulation): every fp32
+// operand x = hi + lo with hi = tf32(x), lo = tf32(x - hi); a product sums
+// lo*hi + hi*lo + hi*hi, which keeps about fp32 accuracy.
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
+  const float r = x - __uint_as_float(hi);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(r));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// d += A B with A (16 x 8) given as fp32 a[4] and B (8 x 8) as fp32 b[2] in the m16n8k8
+// fragment layout (g = lane >> 2, q = lane & 3: a0 (g, q), a1 (g+8, q), a2 (g, q+4),
+// a3 (g+8, q+4); b0 (k = q, n = g), b1 (k = q+4, n = g); d0/d1 (g, 2q / 2q+1),
+// d2/d3 (g+8, 2q / 2q+1)).
+__device__ __forceinline__ void mma3_tf32(float (&d)[4], const float (&a)[4], const float (&b)[2]) {
+  uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) tf32_split(a[i], ah[i], al[i]);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) tf32_split(b[i], bh[i], bl[i]);
+  mma_tf32(d, al, bh);
+  mma_tf32(d, ah, bl);
+  mma_tf32(d, ah, bh);
+}
+
+constexpr int PH_LD = 72;   // padded row strides: conflict-free fragment loads
+constexpr int WQ_LD = 68;
+
+// grid = (max segments, H), block = 256 (8 warps). For every segment of a multi-segment
+// sequence: qt[c] = Q_c Phi_c for each of its chunks and phi[seg] = the whole transfer,
+// with Phi <- diag(gL) Phi + Bt^T (What Phi) per chunk, all products on the tensor cores
+// (3xTF32). The next chunk's record rows travel in registers while one computes.
+__global__ void __launch_bounds__(256) k_seg_phi(const float* __restrict__ rec,
+                                                 const int* __restrict__ chunk_cu,
+                                                 const int* __restrict__ seg_cu, int S,
+                                                 float* __restrict__ qt, float* __restrict__ phi) {
+  RWKV_GRID_DEP_ENTRY();
+  __shared__ __align__(16) float Ph[KD * PH_LD];
+  __shared__ __align__(16) float Am[2 * CL * WQ_LD];   // rows 0..15 What, 16..31 Q
+  __shared__ __align__(16) float Bm[CL * PH_LD];
+  __shared__ __align__(16) float X[CL * PH_LD];
+  __shared__ float gl[KD];
+  const int gs = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
+  if (gs >= seg_cu[S]) return;
+  const int s = seq_of(seg_cu, S, gs);
+  const int nseg = seg_cu[s + 1] - seg_cu[s];
+  if (nseg < 2) return;
+  const int g = gs - seg_cu[s];
+  const int c0 = chunk_cu[s] + g * SEG, c1 = min(chunk_cu[s + 1], c0 + SEG);
+  const int lane = tid & 31, warp = tid >> 5, gq = lane >> 2, q = lane & 3;
+  for (int i = tid; i < KD * KD; i += 256) Ph[(i / KD) * PH_LD + i % KD] = (i / KD == i % KD) ? 1.f : 0.f;
+  float4 nw, nq, nb;
+  float ng = 0.f;
+  auto fetch = [&](int c) {
+    const float* R = rec + ((size_t)c * H + h) * REC;
+    nw = reinterpret_cast<const float4*>(R + OFF_W)[tid];
+    nq = reinterpret_cast<const float4*>(R + OFF_Q)[tid];
+    nb = reinterpret_cast<const float4*>(R + OFF_B)[tid];
+    if (tid < KD) ng = R[OFF_G + tid];
+  };
+  fetch(c0);
+  // step 1 tiles: m-tile (warp >> 2) of [What; Q], n-tiles 2 (warp & 3) and +1
+  const int m1 = warp >> 2, n1 = (warp & 3) * 16;
+  // step 2 tiles: m-tile (warp >> 1) of the 64 key rows, n-tiles 32 (warp & 1) .. +3
+  const int m2 = (warp >> 1) * 16, n2 = (warp & 1) * 32;
+  for (int c = c0; c < c1; ++c) {
+    {
+      const int r = tid >> 4, cc = (tid & 15) * 4;  // record rows are [16][64]
+      *reinterpret_cast<float4*>(Am + r * WQ_LD + cc) = nw;
+      *reinterpret_cast<float4*>(Am + (CL + r) * WQ_LD + cc) = nq;
+      *reinterpret_cast<float4*>(Bm + r * PH_LD + cc) = nb;
+      if (tid < KD) gl[tid] = ng;
+    }
+    __syncthreads();
+    if (c + 1 < c1) fetch(c + 1);
+    // step 1: [What; Q] (32 x 64) x Phi (64 x 64)
+    float d1[2][4] = {};
+#pragma unroll
+    for (int kb = 0; kb < KD; kb += 8) {
+      const float* A = Am + (m1 * 16) * WQ_LD + kb;
+      const float a[4] = {A[gq * WQ_LD + q], A[(gq + 8) * WQ_LD + q], A[gq * WQ_LD + q + 4],
+                          A[(gq + 8) * WQ_LD + q + 4]};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int nb0 = n1 + nt * 8;
+        const float b[2] = {Ph[(kb + q) * PH_LD + nb0 + gq], Ph[(kb + q + 4) * PH_LD + nb0 + gq]};
+        mma3_tf32(d1[nt], a, b);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int col = n1 + nt * 8 + 2 * q;
+      if (m1 == 0) {  // X = What Phi
+        *reinterpret_cast<float2*>(X + gq * PH_LD + col) = make_float2(d1[nt][0], d1[nt][1]);
+        *reinterpret_cast<float2*>(X + (gq + 8) * PH_LD + col) = make_float2(d1[nt][2], d1[nt][3]);
+      } else {        // Q Phi of this chunk
+        float* o = qt + ((size_t)c * H + h) * (CL * KD);
+        *reinterpret_cast<float2*>(o + gq * KD + col) = make_float2(d1[nt][0], d1[nt][1]);
+        *reinterpret_cast<float2*>(o + (gq + 8) * KD + col) = make_float2(d1[nt][2], d1[nt][3]);
+      }
+    }
+    __syncthreads();
+    // step 2: Phi <- diag(gL) Phi + Bt^T X, A[k][t] = Bt[t][k], B[t][j] = X[t][j]
+    float d2[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int col = n2 + nt * 8 + 2 * q;
+      const float g0 = gl[m2 + gq], g8 = gl[m2 + gq + 8];
+      d2[nt][0] = g0 * Ph[(m2 + gq) * PH_LD + col];
+      d2[nt][1] = g0 * Ph[(m2 + gq) * PH_LD + col + 1];
+      d2[nt][2] = g8 * Ph[(m2 + gq + 8) * PH_LD + col];
+      d2[nt][3] = g8 * Ph[(m2 + gq + 8) * PH_LD + col + 1];
+    }
+#pragma unroll
+    for (int kt = 0; kt < CL; kt += 8) {
+      const float a[4] = {Bm[(kt + q) * PH_LD + m2 + gq], Bm[(kt + q) * PH_LD + m2 + gq + 8],
+                          Bm[(kt + q + 4) * PH_LD + m2 + gq], Bm[(kt + q + 4) * PH_LD + m2 + gq + 8]};
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int nb0 = n2 + nt * 8;
+        const float b[2] = {X[(kt + q) * PH_LD + nb0 + gq], X[(kt + q + 4) * PH_LD + nb0 + gq]};
+        mma3_tf32(d2[nt], a, b);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int col = n2 + nt * 8 + 2 * q;
+      *reinterpret_cast<float2*>(Ph + (m2 + gq) * PH_LD + col) = make_float2(d2[nt][0], d2[nt][1]);
+      *reinterpret_cast<float2*>(Ph + (m2 + gq + 8) * PH_LD + col) = make_float2(d2[nt][2], d2[nt][3]);
+    }
+    __syncthreads();
+  }
+  float* out = phi + ((size_t)gs * H + h) * (KD * KD);
+  for (int i = tid; i < KD * KD / 4; i += 256) {
+    const int r = i / (KD / 4), cc = (i % (KD / 4)) * 4;
+    reinterpret_cast<float4*>(out)[i] = *reinterpret_cast<const float4*>(Ph + r * PH_LD + cc);
+  }
+}
+
+// grid = (S, H, 4 row quarters), block = 256. Walks a multi-segment sequence's segments
+// in order: the true start of segment g + 1 is phi[g] applied to the true start of g
+// plus g's zero-start end state (segment 0's end state, scanned from the true state,
+// is already the true start of segment 1). Start states go to sst for k_seg_fix; the final state
+// to rnn. Thread: key k = tid & 63, rows 4 (tid >> 6) .. +3 of the quarter.
+__global__ void __launch_bounds__(256) k_seg_combine(const int* __restrict__ seg_cu,
+                                                     const int* __restrict__ slots,
+                                                     const float* __restrict__ lbuf,
+                                                     const float* __restrict__ phi,
+                                                     float* __restrict__ sst,
+                                                     float* __restrict__ rnn) {
+  RWKV_GRID_DEP_ENTRY();
+  __shared__ float Ps[KD][KD + 1];   // Phi, padded: lanes walk rows k at a common column j
+  __shared__ float Sm[16][KD];       // the quarter's 16 state rows
+  const int s = blockIdx.x, h = blockIdx.y, H = gridDim.y, q = blockIdx.z, tid = threadIdx.x;
+  const int seg0 = seg_cu[s], nseg = seg_cu[s + 1] - seg0;
+  if (nseg < 2) return;
+  const int slot = slots ? slots[s] : s;
+  const int k = tid & 63, v0 = (tid >> 6) * 4;  // rows v0..v0+3 of the quarter
+  const size_t rbase = (size_t)(q * 16) * KD;   // first row of the quarter
+  auto seg_off = [&](int g) { return ((size_t)(seg0 + g) * H + h) * KD * KD; };
+  float st[4], pl[4], pp[16];  // state; prefetched L_g and Phi_g of the next step
+  const size_t o0 = seg_off(0);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) st[e] = lbuf[o0 + rbase + (v0 + e) * KD + k];
+  auto fetch = [&](int g) {
+    const size_t so = seg_off(g);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pl[e] = lbuf[so + rbase + (v0 + e) * KD + k];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pp[i] = phi[so + tid + 256 * i];
+  };
+  fetch(1);
+  for (int g = 1; g < nseg; ++g) {
+    const size_t so = seg_off(g);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      sst[so + rbase + (v0 + e) * KD + k] = st[e];
+      Sm[v0 + e][k] = st[e];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int idx = tid + 256 * i;
+      Ps[idx / KD][idx % KD] = pp[i];
+    }
+    float acc[4] = {pl[0], pl[1], pl[2], pl[3]};
+    __syncthreads();
+    if (g + 1 < nseg) fetch(g + 1);
+    // start of segment g + 1 = Phi_g (start of g) + (g's zero-start end state)
+#pragma unroll 8
+    for (int j = 0; j < KD; ++j) {
+      const float p = Ps[k][j];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] += p * Sm[v0 + e][j];
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) st[e] = acc[e];
+    __syncthreads();
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) rnn[(((size_t)slot * H + h) * KD) * KD + rbase + (v0 + e) * KD + k] = st[e];
+}
+
+// grid = (max segments, H), block = 256 (8 warps). Segments g >= 1 of multi-segment
+// sequences: for each chunk, y = yf32 + (Q Phi) S_g^T on the tensor cores (3xTF32),
+// rounded to fp16 once (like the reference's y store). Warp w owns state rows 8w..8w+7;
+// S_g is loaded once per segment, the next chunk's Q Phi is prefetched into registers.
+__global__ void __launch_bounds__(256) k_seg_fix(const int* __restrict__ cu,
+                                                 const int* __restrict__ chunk_cu,
+                                                 const int* __restrict__ seg_cu, int S,
+                                                 const float* __restrict__ qt,
+                                                 const float* __restrict__ sst,
+                                                 const float* __restrict__ yf32,
+                                                 __half* __restrict__ ybuf, int C) {
+  RWKV_GRID_DEP_ENTRY();
+  __shared__ __align__(16) float Ss[KD * WQ_LD];
+  __shared__ __align__(16) float Qs[CL * WQ_LD];
+  const int gs = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
+  if (gs >= seg_cu[S]) return;
+  const int s = seq_of(seg_cu, S, gs);
+  const int nseg = seg_cu[s + 1] - seg_cu[s], g = gs - seg_cu[s];
+  if (nseg < 2 || g == 0) return;
+  const int c0 = chunk_cu[s] + g * SEG, c1 = min(chunk_cu[s + 1], c0 + SEG);
+  const size_t so = ((size_t)gs * H + h) * KD * KD;
+  for (int i = tid; i < KD * KD / 4; i += 256) {
+    const int r = i / (KD / 4), cc = (i % (KD / 4)) * 4;
+    *reinterpret_cast<float4*>(Ss + r * WQ_LD + cc) = reinterpret_cast<const float4*>(sst + so)[i];
+  }
+  const int lane = tid & 31, warp = tid >> 5, gq = lane >> 2, q = lane & 3;
+  const int m_end = cu[s + 1];
+  float4 nq = reinterpret_cast<const float4*>(qt + ((size_t)c0 * H + h) * (CL * KD))[tid];
+  for (int c = c0; c < c1; ++c) {
+    *reinterpret_cast<float4*>(Qs + (tid >> 4) * WQ_LD + (tid & 15) * 4) = nq;
+    __syncthreads();
+    if (c + 1 < c1) nq = reinterpret_cast<const float4*>(qt + ((size_t)(c + 1) * H + h) * (CL * KD))[tid];
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    const int nb0 = warp * 8;
+#pragma unroll
+    for (int kb = 0; kb < KD; kb += 8) {
+      const float a[4] = {Qs[gq * WQ_LD + kb + q], Qs[(gq + 8) * WQ_LD + kb + q],
+                          Qs[gq * WQ_LD + kb + q + 4], Qs[(gq + 8) * WQ_LD + kb + q + 4]};
+      const float b[2] = {Ss[(nb0 + gq) * WQ_LD + kb + q], Ss[(nb0 + gq) * WQ_LD + kb + q + 4]};
+      mma3_tf32(d, a, b);
+    }
+    const int m0 = cu[s] + (c - chunk_cu[s]) * CL;
+    const int v = nb0 + 2 * q;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int m = m0 + gq + 8 * half;
+      if (m < m_end) {
+        const size_t o = (size_t)m * C + h * KD + v;
+        const float2 yv = *reinterpret_cast<const float2*>(yf32 + o);
+        *reinterpret_cast<__half2*>(ybuf + o) =
+            __floats2half2_rn(yv.x + d[2 * half], yv.y + d[2 * half + 1]);
+      }
+    }
+    __syncthreads();
+  }
 }
 
 // Per-head GroupNorm + bonus + g gate on precomputed y (one warp per head and row).
@@ -487,27 +805,61 @@ __global__ void k_wkv_epilogue(const __half* __restrict__ ybuf, const __half* __
   *reinterpret_cast<__half2*>(yg + o) = __floats2half2_rn(ox * gg.x, oy * gg.y);
 }
 
+// Scratch of the chunked recurrence (floats, in this order): chunk records [chunks][H][REC],
+// Q Phi per chunk [chunks][H][16 x 64], per segment the zero-start end state, the
+// transfer Phi and the true start state [segments][H][64 x 64] each, fp32 outputs
+// [M][C], then the segment table (S + 1 ints). chunks <= M/16 + S, segments <= M/256 + S.
+struct ChunkScratch {
+  float *rec, *qt, *lbuf, *phi, *sst, *yf32;
+  int* seg_cu;
+};
+namespace {
+size_t pad64(size_t n) { return (n + 63) & ~size_t(63); }
+ChunkScratch chunk_scratch(float* base, int M, int S, int H, size_t* total_floats) {
+  const size_t maxc = (size_t)M / CL + S, maxs = (size_t)M / (CL * SEG) + S;
+  ChunkScratch c;
+  size_t o = 0;
+  c.rec = base + o;  o += pad64(maxc * H * REC);
+  c.qt = base + o;   o += pad64(maxc * H * CL * KD);
+  c.lbuf = base + o; o += pad64(maxs * H * KD * KD);
+  c.phi = base + o;  o += pad64(maxs * H * KD * KD);
+  c.sst = base + o;  o += pad64(maxs * H * KD * KD);
+  c.yf32 = base + o; o += pad64((size_t)M * H * KD);
+  c.seg_cu = reinterpret_cast<int*>(base + o); o += pad64((size_t)S + 1);
+  if (total_floats) *total_floats = o;
+  return c;
+}
+}  // namespace
+
 size_t wkv_chunk_record_bytes(int M, int S, int H) {
-  return ((size_t)(M / CL + S) * H * REC) * sizeof(float);
+  size_t n = 0;
+  chunk_scratch(nullptr, M, S, H, &n);
+  return n * sizeof(float);
 }
 
 // Chunked recurrence only: y (fp16) for every row, state updated in place.
 // r..b, y: [M, C] rows (C = H * 64); rnn: [slots, H, 64, 64].
-// chunk_cu[s] = chunks before sequence s; depends on the sequence table only, so a
-// forward computes it once for all layers.
-int launch_chunk_table(const int* cu, int* chunk_cu, int S, cudaStream_t st) {
-  return rwkv_launch("chunk_table", k_chunk_table, dim3(1), dim3(1024), 0, st, cu, chunk_cu, S);
+// chunk_cu[s] / seg_cu[s] = chunks / segments before sequence s; they depend on the
+// sequence table only, so a forward computes them once for all layers. `rec` is the
+// chunk scratch (wkv_chunk_record_bytes(M, S, H) bytes).
+int launch_chunk_table(const int* cu, int* chunk_cu, float* rec, int M, int S, int H,
+                       cudaStream_t st) {
+  const ChunkScratch cs = chunk_scratch(rec, M, S, H, nullptr);
+  return rwkv_launch("chunk_table", k_chunk_table, dim3(1), dim3(1024), 0, st, cu, chunk_cu,
+                     cs.seg_cu, S);
 }
 
-// Chunk transforms + scan of one layer; `chunk_cu` must already hold the chunk table.
+// Chunk transforms + two-level scan of one layer; the tables must already be built.
 int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const __half* v,
                        const __half* a, const __half* b, float* rnn, const int* cu,
                        const int* slots, __half* ybuf, float* rec, int* chunk_cu, int M, int S,
                        int H, int n_slots, cudaStream_t st) {
   const int C = H * KD;
+  const ChunkScratch cs = chunk_scratch(rec, M, S, H, nullptr);
+  const int maxc = M / CL + S, maxs = M / (CL * SEG) + S;
   int rc;
-  if ((rc = rwkv_launch("chunk_prep", k_chunk_prep, dim3(M / CL + S, H), dim3(256), 0, st, r, w, k,
-                        v, a, b, cu, chunk_cu, S, C, M, rec)))
+  if ((rc = rwkv_launch("chunk_prep", k_chunk_prep, dim3(maxc, H), dim3(256), 0, st, r, w, k,
+                        v, a, b, cu, chunk_cu, S, C, M, cs.rec)))
     return rc;
   static bool attr_done[64] = {};
   int dev = 0;
@@ -521,8 +873,21 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
     }
     attr_done[dev] = true;
   }
-  return rwkv_launch("chunk_scan", k_chunk_scan, dim3(S, H, KD / SCAN_ROWS), dim3(SCAN_THREADS), SCAN_SMEM,
-                     st, rec, cu, chunk_cu, slots, rnn, ybuf, C, M, M / CL + S, n_slots);
+  // plain launch: thousands of early-placed segment CTAs would crowd the SMs prep runs on
+  rwkv_chain_begin();
+  if ((rc = rwkv_launch("chunk_scan", k_chunk_scan, dim3(maxs, H, KD / SCAN_ROWS),
+                        dim3(SCAN_THREADS), SCAN_SMEM, st, cs.rec, cu, chunk_cu, cs.seg_cu, slots,
+                        rnn, ybuf, cs.yf32, cs.lbuf, S, C, M, maxc, n_slots)))
+    return rc;
+  rwkv_chain_begin();
+  if ((rc = rwkv_launch("seg_phi", k_seg_phi, dim3(maxs, H), dim3(256), 0, st, cs.rec, chunk_cu,
+                        cs.seg_cu, S, cs.qt, cs.phi)))
+    return rc;
+  if ((rc = rwkv_launch("seg_combine", k_seg_combine, dim3(S, H, 4), dim3(256), 0, st, cs.seg_cu,
+                        slots, cs.lbuf, cs.phi, cs.sst, rnn)))
+    return rc;
+  return rwkv_launch("seg_fix", k_seg_fix, dim3(maxs, H), dim3(256), 0, st, cu, chunk_cu,
+                     cs.seg_cu, S, cs.qt, cs.sst, cs.yf32, ybuf, C);
 }
 
 int launch_wkv_epilogue(int sem, const __half* ybuf, const __half* rbuf, const __half* gbuf,
@@ -586,7 +951,7 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
   int rc = rwkv_launch("uniform_cu", k_uniform_cu, dim3((n_seq + 256) / 256), dim3(256), 0, st, cu,
                        n_seq, T);
   if (rc) return rc;
-  if ((rc = launch_chunk_table(cu, chunk_cu, n_seq, st))) return rc;
+  if ((rc = launch_chunk_table(cu, chunk_cu, rec, n_seq * T, n_seq, H, st))) return rc;
   return launch_wkv_chunked((const __half*)r, (const __half*)w, (const __half*)k,
                             (const __half*)v, (const __half*)a, (const __half*)b, (float*)S, cu,
                             nullptr, (__half*)y, rec, chunk_cu, n_seq * T, n_seq, H, n_seq, st);
