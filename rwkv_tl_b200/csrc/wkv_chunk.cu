@@ -358,16 +358,14 @@ static_assert((SHARED_F * 4) % 16 == 0 && (SLICE_F * 4) % 16 == 0 && (REC * 4) %
 // PU v / PY v that k_chunk_prep precomputed, writes y (fp16, rounded like the
 // reference's y store) to ybuf [M, C] and advances the fp32 state by
 //   s <- s * gL + sum_j sa_j Bt_j + U.
-__global__ void __launch_bounds__(SCAN_THREADS) k_chunk_scan(
+__device__ __forceinline__ void chunk_scan_body(
+    int gs, int h, int H, int grp, float* scan_smem,
     const float* __restrict__ rec, const int* __restrict__ cu, const int* __restrict__ chunk_cu,
     const int* __restrict__ seg_cu, const int* __restrict__ slots, float* __restrict__ rnn,
     __half* __restrict__ ybuf, float* __restrict__ yf32, float* __restrict__ lbuf, int S, int C,
     int M, int max_chunks, int n_slots) {
-  RWKV_GRID_DEP_ENTRY();
-  extern __shared__ __align__(128) float scan_smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(scan_smem + (size_t)NSTAGE * STAGE_F);
   uint64_t* empty = full + NSTAGE;
-  const int gs = blockIdx.x, h = blockIdx.y, H = gridDim.y, grp = blockIdx.z;
   if (gs >= seg_cu[S]) return;
   const int s = seq_of(seg_cu, S, gs);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -540,17 +538,17 @@ constexpr int WQ_LD = 68;
 // sequence: qt[c] = Q_c Phi_c for each of its chunks and phi[seg] = the whole transfer,
 // with Phi <- diag(gL) Phi + Bt^T (What Phi) per chunk, all products on the tensor cores
 // (3xTF32). The next chunk's record rows travel in registers while one computes.
-__global__ void __launch_bounds__(256) k_seg_phi(const float* __restrict__ rec,
-                                                 const int* __restrict__ chunk_cu,
-                                                 const int* __restrict__ seg_cu, int S,
-                                                 float* __restrict__ qt, float* __restrict__ phi) {
-  RWKV_GRID_DEP_ENTRY();
-  __shared__ __align__(16) float Ph[KD * PH_LD];
-  __shared__ __align__(16) float Am[2 * CL * WQ_LD];   // rows 0..15 What, 16..31 Q
-  __shared__ __align__(16) float Bm[CL * PH_LD];
-  __shared__ __align__(16) float X[CL * PH_LD];
-  __shared__ float gl[KD];
-  const int gs = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
+__device__ __forceinline__ void seg_phi_body(int gs, int h, int H, float* smem,
+                                             const float* __restrict__ rec,
+                                             const int* __restrict__ chunk_cu,
+                                             const int* __restrict__ seg_cu, int S,
+                                             float* __restrict__ qt, float* __restrict__ phi) {
+  float* Ph = smem;                          // [64][PH_LD]
+  float* Am = Ph + KD * PH_LD;               // [32][WQ_LD]: rows 0..15 What, 16..31 Q
+  float* Bm = Am + 2 * CL * WQ_LD;           // [16][PH_LD]
+  float* X = Bm + CL * PH_LD;                // [16][PH_LD]
+  float* gl = X + CL * PH_LD;                // [64]
+  const int tid = threadIdx.x;
   if (gs >= seg_cu[S]) return;
   const int s = seq_of(seg_cu, S, gs);
   const int nseg = seg_cu[s + 1] - seg_cu[s];
@@ -645,6 +643,32 @@ __global__ void __launch_bounds__(256) k_seg_phi(const float* __restrict__ rec,
     const int r = i / (KD / 4), cc = (i % (KD / 4)) * 4;
     reinterpret_cast<float4*>(out)[i] = *reinterpret_cast<const float4*>(Ph + r * PH_LD + cc);
   }
+}
+
+static_assert(KD * PH_LD + 2 * CL * WQ_LD + 2 * CL * PH_LD + KD <= NSTAGE * STAGE_F,
+              "the transfer-matrix blocks fit the scan's shared memory");
+
+// One launch, two roles, because the transfer matrices need only the chunk records:
+// blocks [0, n_phi) are (segment, head) transfer-matrix blocks (seg_phi_body, tensor
+// pipe), the rest are (segment, head, row group) scan blocks (chunk_scan_body, a
+// latency-bound chain); sharing the SMs, the first hide under the second.
+__global__ void __launch_bounds__(SCAN_THREADS, 4) k_scan_phi(
+    const float* __restrict__ rec, const int* __restrict__ cu, const int* __restrict__ chunk_cu,
+    const int* __restrict__ seg_cu, const int* __restrict__ slots, float* __restrict__ rnn,
+    __half* __restrict__ ybuf, float* __restrict__ yf32, float* __restrict__ lbuf,
+    float* __restrict__ qt, float* __restrict__ phi, int S, int H, int C, int M, int max_chunks,
+    int n_slots, int n_phi) {
+  RWKV_GRID_DEP_ENTRY();
+  extern __shared__ __align__(128) float smem[];
+  const int bx = blockIdx.x;
+  if (bx < n_phi) {
+    seg_phi_body(bx / H, bx % H, H, smem, rec, chunk_cu, seg_cu, S, qt, phi);
+    return;
+  }
+  constexpr int G = KD / SCAN_ROWS;
+  const int b = bx - n_phi, gs = b / (H * G), rem = b % (H * G);
+  chunk_scan_body(gs, rem / G, H, rem % G, smem, rec, cu, chunk_cu, seg_cu, slots, rnn, ybuf,
+                  yf32, lbuf, S, C, M, max_chunks, n_slots);
 }
 
 // grid = (S, H, 4 row quarters), block = 256. Walks a multi-segment sequence's segments
@@ -865,7 +889,7 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_chunk_scan, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_scan_phi, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)SCAN_SMEM);
     if (e != cudaSuccess) {
       rwkv_set_error("chunk_scan: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -875,13 +899,11 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   }
   // plain launch: thousands of early-placed segment CTAs would crowd the SMs prep runs on
   rwkv_chain_begin();
-  if ((rc = rwkv_launch("chunk_scan", k_chunk_scan, dim3(maxs, H, KD / SCAN_ROWS),
+  const int n_phi = maxs * H;
+  if ((rc = rwkv_launch("scan_phi", k_scan_phi, dim3(n_phi + maxs * H * (KD / SCAN_ROWS)),
                         dim3(SCAN_THREADS), SCAN_SMEM, st, cs.rec, cu, chunk_cu, cs.seg_cu, slots,
-                        rnn, ybuf, cs.yf32, cs.lbuf, S, C, M, maxc, n_slots)))
-    return rc;
-  rwkv_chain_begin();
-  if ((rc = rwkv_launch("seg_phi", k_seg_phi, dim3(maxs, H), dim3(256), 0, st, cs.rec, chunk_cu,
-                        cs.seg_cu, S, cs.qt, cs.phi)))
+                        rnn, ybuf, cs.yf32, cs.lbuf, cs.qt, cs.phi, S, H, C, M, maxc, n_slots,
+                        n_phi)))
     return rc;
   if ((rc = rwkv_launch("seg_combine", k_seg_combine, dim3(S, H, 4), dim3(256), 0, st, cs.seg_cu,
                         slots, cs.lbuf, cs.phi, cs.sst, rnn)))
