@@ -766,8 +766,18 @@ __global__ void __launch_bounds__(256) k_seg_fix(const int* __restrict__ cu,
     *reinterpret_cast<float4*>(Qs + (tid >> 4) * WQ_LD + (tid & 15) * 4) = nq;
     __syncthreads();
     if (c + 1 < c1) nq = reinterpret_cast<const float4*>(qt + ((size_t)(c + 1) * H + h) * (CL * KD))[tid];
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
     const int nb0 = warp * 8;
+    const int m0 = cu[s] + (c - chunk_cu[s]) * CL;
+    const int v = nb0 + 2 * q;
+    // this chunk's fp32 partial outputs, fetched before the products (latency overlap)
+    float2 yv[2];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int m = m0 + gq + 8 * half;
+      yv[half] = m < m_end ? *reinterpret_cast<const float2*>(yf32 + (size_t)m * C + h * KD + v)
+                           : make_float2(0.f, 0.f);
+    }
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int kb = 0; kb < KD; kb += 8) {
       const float a[4] = {Qs[gq * WQ_LD + kb + q], Qs[(gq + 8) * WQ_LD + kb + q],
@@ -775,17 +785,12 @@ __global__ void __launch_bounds__(256) k_seg_fix(const int* __restrict__ cu,
       const float b[2] = {Ss[(nb0 + gq) * WQ_LD + kb + q], Ss[(nb0 + gq) * WQ_LD + kb + q + 4]};
       mma3_tf32(d, a, b);
     }
-    const int m0 = cu[s] + (c - chunk_cu[s]) * CL;
-    const int v = nb0 + 2 * q;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int m = m0 + gq + 8 * half;
-      if (m < m_end) {
-        const size_t o = (size_t)m * C + h * KD + v;
-        const float2 yv = *reinterpret_cast<const float2*>(yf32 + o);
-        *reinterpret_cast<__half2*>(ybuf + o) =
-            __floats2half2_rn(yv.x + d[2 * half], yv.y + d[2 * half + 1]);
-      }
+      if (m < m_end)
+        *reinterpret_cast<__half2*>(ybuf + (size_t)m * C + h * KD + v) =
+            __floats2half2_rn(yv[half].x + d[2 * half], yv[half].y + d[2 * half + 1]);
     }
     __syncthreads();
   }
