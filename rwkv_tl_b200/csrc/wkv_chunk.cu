@@ -334,8 +334,8 @@ __device__ __forceinline__ float dot4(float4 a, float2 s01, float2 s23) {
   return p.x + p.y;
 }
 
-constexpr int SCAN_ROWS = 16;                       // state rows per CTA
-constexpr int SCAN_THREADS = 256;                   // eight warps, two rows each
+constexpr int SCAN_ROWS = 32;                       // state rows per CTA
+constexpr int SCAN_THREADS = 256;                   // eight warps, four rows each
 constexpr int SLICE_F = SCAN_ROWS * RWS;            // per-CTA part of a record's row terms
 constexpr int STAGE_F = SHARED_F + SLICE_F;         // floats per ring stage
 // Chunk records in flight per CTA: a segment has at most SEG chunks and several
@@ -369,8 +369,8 @@ __device__ __forceinline__ void chunk_scan_body(
   if (gs >= seg_cu[S]) return;
   const int s = seq_of(seg_cu, S, gs);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hl = lane & 15, lrow = warp * 2 + (lane >> 4);
-  const int row = grp * SCAN_ROWS + lrow;
+  const int hl = lane & 15, lrow0 = warp * 4 + (lane >> 4) * 2;  // rows lrow0, lrow0 + 1
+  const int row0 = grp * SCAN_ROWS + lrow0;
   const int slot = slots ? slots[s] : s;
   const int cs = chunk_cu[s], ce = chunk_cu[s + 1];
   const int nseg = seg_cu[s + 1] - seg_cu[s], g = gs - seg_cu[s];
@@ -392,8 +392,16 @@ __device__ __forceinline__ void chunk_scan_body(
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  float* Srow = rnn + (((size_t)slot * H + h) * KD + row) * KD + 4 * hl;
-  float4 st = g == 0 ? *reinterpret_cast<const float4*>(Srow) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float* Srow = rnn + (((size_t)slot * H + h) * KD + row0) * KD + 4 * hl;
+  float4 st0 = make_float4(0.f, 0.f, 0.f, 0.f), st1 = st0;
+  if (g == 0) {
+    st0 = *reinterpret_cast<const float4*>(Srow);
+    st1 = *reinterpret_cast<const float4*>(Srow + KD);
+  }
+  // the lane's four reduced sums: row my_row, outputs (my_y) or in-chunk states, t = my_t..+3
+  const int my_row = hl < 8 ? row0 : row0 + 1, my_lrow = hl < 8 ? lrow0 : lrow0 + 1;
+  const bool my_y = hl & 4;
+  const int my_t = (4 * hl) & 15;
   int issued = 0;  // chunks whose copies thread 0 has issued
   auto issue = [&](int c) {
     const int buf = (c - c0) % NSTAGE;
@@ -417,17 +425,23 @@ __device__ __forceinline__ void chunk_scan_body(
     ok = __all_sync(0xffffffffu, ok && sc_mbar_wait(&full[buf], (it / NSTAGE) & 1));
     if (!ok) break;
     const float* R = scan_smem + (size_t)buf * STAGE_F;
-    const float* RW = R + SHARED_F + lrow * RWS;
-    const float2 s01 = make_float2(st.x, st.y), s23 = make_float2(st.z, st.w);
-    float p[32];
+    const float* RW = R + SHARED_F;
+    const float2 a01 = make_float2(st0.x, st0.y), a23 = make_float2(st0.z, st0.w);
+    const float2 b01 = make_float2(st1.x, st1.y), b23 = make_float2(st1.z, st1.w);
+    // each What / Q load serves both rows of the half-warp
+    float p[64];
 #pragma unroll
     for (int t = 0; t < CL; ++t) {
-      p[t] = dot4(*reinterpret_cast<const float4*>(R + OFF_W + t * KD + 4 * hl), s01, s23);
-      p[CL + t] = dot4(*reinterpret_cast<const float4*>(R + OFF_Q + t * KD + 4 * hl), s01, s23);
+      const float4 w = *reinterpret_cast<const float4*>(R + OFF_W + t * KD + 4 * hl);
+      const float4 q = *reinterpret_cast<const float4*>(R + OFF_Q + t * KD + 4 * hl);
+      p[t] = dot4(w, a01, a23);
+      p[CL + t] = dot4(q, a01, a23);
+      p[2 * CL + t] = dot4(w, b01, b23);
+      p[3 * CL + t] = dot4(q, b01, b23);
     }
-    // transpose-reduce over the 16 lanes of the half-warp: 32 -> 16 -> 8 -> 4 -> 2 sums
+    // transpose-reduce over the 16 lanes of the half-warp: 64 -> 32 -> 16 -> 8 -> 4 sums
 #pragma unroll
-    for (int m = 8, half = 16; m >= 1; m >>= 1, half >>= 1) {
+    for (int m = 8, half = 32; m >= 1; m >>= 1, half >>= 1) {
       const bool up = lane & m;
 #pragma unroll
       for (int i = 0; i < half; ++i) {
@@ -436,43 +450,43 @@ __device__ __forceinline__ void chunk_scan_body(
         p[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
       }
     }
-    // lane hl holds sums 2hl, 2hl + 1: (What s)_t for hl < 8, (Q s)_t for hl >= 8, t = 2hl mod 16
-    const float2 add = *reinterpret_cast<const float2*>(RW + 2 * hl);
-    const float o0 = p[0] + add.x, o1 = p[1] + add.y;
-    if (hl >= 8) {
-      const int m0 = m_beg + it * CL + 2 * hl - CL;
-      if (g == 0) {  // final outputs
-        __half* yp = ybuf + (size_t)m0 * C + h * KD + row;
-        if (m0 < m_end) yp[0] = f2h(o0);
-        if (m0 + 1 < m_end) yp[C] = f2h(o1);
-      } else {  // partial outputs: k_seg_fix adds the incoming state's part
-        float* yp = yf32 + (size_t)m0 * C + h * KD + row;
-        if (m0 < m_end) yp[0] = o0;
-        if (m0 + 1 < m_end) yp[C] = o1;
+    // lane hl holds sums 4hl..4hl+3 (What s or Q s of row my_row); add PU v / PY v
+    const float4 add = *reinterpret_cast<const float4*>(RW + my_lrow * RWS + ((4 * hl) & 31));
+    const float4 o = make_float4(p[0] + add.x, p[1] + add.y, p[2] + add.z, p[3] + add.w);
+    if (my_y) {
+      const int m0 = m_beg + it * CL + my_t;
+      const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (m0 + e >= m_end) break;
+        const size_t off = (size_t)(m0 + e) * C + h * KD + my_row;
+        if (g == 0) ybuf[off] = f2h(ov[e]);   // final outputs
+        else yf32[off] = ov[e];                // partial: k_seg_fix adds the incoming state's part
       }
     }
     const float4 gl = *reinterpret_cast<const float4*>(R + OFF_G + 4 * hl);
-    const float4 u = *reinterpret_cast<const float4*>(RW + 2 * CL + 4 * hl);
-    float2 n01 = __ffma2_rn(s01, make_float2(gl.x, gl.y), make_float2(u.x, u.y));
-    float2 n23 = __ffma2_rn(s23, make_float2(gl.z, gl.w), make_float2(u.z, u.w));
-    float2 m01 = make_float2(0.f, 0.f), m23 = make_float2(0.f, 0.f);
-    const int src = lane & 16;
+    const float4 u0 = *reinterpret_cast<const float4*>(RW + lrow0 * RWS + 2 * CL + 4 * hl);
+    const float4 u1 = *reinterpret_cast<const float4*>(RW + (lrow0 + 1) * RWS + 2 * CL + 4 * hl);
+    const float2 g01 = make_float2(gl.x, gl.y), g23 = make_float2(gl.z, gl.w);
+    float2 n01 = __ffma2_rn(a01, g01, make_float2(u0.x, u0.y));
+    float2 n23 = __ffma2_rn(a23, g23, make_float2(u0.z, u0.w));
+    float2 m01 = __ffma2_rn(b01, g01, make_float2(u1.x, u1.y));
+    float2 m23 = __ffma2_rn(b23, g23, make_float2(u1.z, u1.w));
+    const int src0 = lane & 16, src1 = src0 + 8;  // lanes holding the states of row 0 / row 1
 #pragma unroll
     for (int j = 0; j < CL; ++j) {
-      const float sa = __shfl_sync(0xffffffffu, (j & 1) ? o1 : o0, src + (j >> 1));
+      const float v = (j & 3) == 0 ? o.x : (j & 3) == 1 ? o.y : (j & 3) == 2 ? o.z : o.w;
+      const float sa0 = __shfl_sync(0xffffffffu, v, src0 + (j >> 2));
+      const float sa1 = __shfl_sync(0xffffffffu, v, src1 + (j >> 2));
       const float4 b = *reinterpret_cast<const float4*>(R + OFF_B + j * KD + 4 * hl);
-      const float2 sa2 = make_float2(sa, sa);
-      if (j & 1) {
-        m01 = __ffma2_rn(sa2, make_float2(b.x, b.y), m01);
-        m23 = __ffma2_rn(sa2, make_float2(b.z, b.w), m23);
-      } else {
-        n01 = __ffma2_rn(sa2, make_float2(b.x, b.y), n01);
-        n23 = __ffma2_rn(sa2, make_float2(b.z, b.w), n23);
-      }
+      const float2 bl = make_float2(b.x, b.y), bh = make_float2(b.z, b.w);
+      n01 = __ffma2_rn(make_float2(sa0, sa0), bl, n01);
+      n23 = __ffma2_rn(make_float2(sa0, sa0), bh, n23);
+      m01 = __ffma2_rn(make_float2(sa1, sa1), bl, m01);
+      m23 = __ffma2_rn(make_float2(sa1, sa1), bh, m23);
     }
-    n01 = __fadd2_rn(n01, m01);
-    n23 = __fadd2_rn(n23, m23);
-    st = make_float4(n01.x, n01.y, n23.x, n23.y);
+    st0 = make_float4(n01.x, n01.y, n23.x, n23.y);
+    st1 = make_float4(m01.x, m01.y, m23.x, m23.y);
     __syncwarp();
     if (lane == 0) sc_mbar_arrive(&empty[buf]);
   }
@@ -487,10 +501,9 @@ __device__ __forceinline__ void chunk_scan_body(
       }
     return;
   }
-  if (nseg == 1)
-    *reinterpret_cast<float4*>(Srow) = st;
-  else
-    *reinterpret_cast<float4*>(lbuf + (((size_t)gs * H + h) * KD + row) * KD + 4 * hl) = st;
+  float* dst = nseg == 1 ? Srow : lbuf + (((size_t)gs * H + h) * KD + row0) * KD + 4 * hl;
+  *reinterpret_cast<float4*>(dst) = st0;
+  *reinterpret_cast<float4*>(dst + KD) = st1;
 }
 
 // ---- two-level scan: segment transfers, the cross-segment pass, output correction ----
@@ -652,7 +665,7 @@ static_assert(KD * PH_LD + 2 * CL * WQ_LD + 2 * CL * PH_LD + KD <= NSTAGE * STAG
 // blocks [0, n_phi) are (segment, head) transfer-matrix blocks (seg_phi_body, tensor
 // pipe), the rest are (segment, head, row group) scan blocks (chunk_scan_body, a
 // latency-bound chain); sharing the SMs, the first hide under the second.
-__global__ void __launch_bounds__(SCAN_THREADS, 4) k_scan_phi(
+__global__ void __launch_bounds__(SCAN_THREADS, 3) k_scan_phi(
     const float* __restrict__ rec, const int* __restrict__ cu, const int* __restrict__ chunk_cu,
     const int* __restrict__ seg_cu, const int* __restrict__ slots, float* __restrict__ rnn,
     __half* __restrict__ ybuf, float* __restrict__ yf32, float* __restrict__ lbuf,
