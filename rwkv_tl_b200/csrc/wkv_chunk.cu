@@ -34,6 +34,9 @@ constexpr int REC = SHARED_F + KD * RWS;      // floats per (chunk, head) record
 constexpr int OFF_W = 0, OFF_Q = CL * KD, OFF_B = 2 * CL * KD, OFF_G = 3 * CL * KD,
               OFF_RW = SHARED_F;
 constexpr int RS = KD + 1;  // padded smem row stride (conflict-free column walks)
+#ifndef PREP_MINB
+#define PREP_MINB 6
+#endif
 // Two-level scan: a sequence's chunks are cut into segments of SEG chunks (256 tokens).
 // Segments are scanned concurrently (the first from the true state, the others from
 // zero); each segment's transfer matrix Phi (product of its chunk maps) then carries
@@ -93,7 +96,7 @@ __device__ __forceinline__ int seq_of(const int* tab, int S, int x) {
 
 // grid = (max_chunks, H), block = 256. Rows past the sequence end are padded
 // with identity transitions (w = 1, a = b = k = r = 0).
-__global__ void __launch_bounds__(256, 4) k_chunk_prep(
+__global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
     const __half* __restrict__ rb, const __half* __restrict__ wb, const __half* __restrict__ kb,
     const __half* __restrict__ vb, const __half* __restrict__ ab, const __half* __restrict__ bb,
     const int* __restrict__ cu,
@@ -149,16 +152,16 @@ __global__ void __launch_bounds__(256, 4) k_chunk_prep(
   __syncthreads();
   // 2. cumulative log decay per column, then decay-scaled vectors
   if (tid < KD) {
-    float g = 0.f;
+    float g = 0.f, egp = 1.f;  // e^{G_{t-1}}, carried
     for (int t = 0; t < CL; ++t) {
-      const float gprev = g;
       g += sg[t * RS + tid];
-      const float eg = expf(g), egi = expf(-g), egp = expf(gprev);
+      const float eg = expf(g), egi = 1.0f / eg;
       sa_[t * RS + tid] *= egp;
       sb_[t * RS + tid] *= egi;
       sk_[t * RS + tid] *= egi;
       sr_[t * RS + tid] *= eg;
       sg[t * RS + tid] = g;
+      egp = eg;
     }
     glv[tid] = expf(g);
   }
