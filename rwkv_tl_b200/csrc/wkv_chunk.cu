@@ -35,7 +35,7 @@ constexpr int OFF_W = 0, OFF_Q = CL * KD, OFF_B = 2 * CL * KD, OFF_G = 3 * CL * 
               OFF_RW = SHARED_F;
 constexpr int RS = KD + 1;  // padded smem row stride (conflict-free column walks)
 #ifndef PREP_MINB
-#define PREP_MINB 6
+#define PREP_MINB 7
 #endif
 // Two-level scan: a sequence's chunks are cut into segments of SEG chunks (256 tokens).
 // Segments are scanned concurrently (the first from the true state, the others from
@@ -104,10 +104,13 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
   RWKV_GRID_DEP_ENTRY();
   __shared__ float sa_[CL * RS], sb_[CL * RS], sk_[CL * RS], sr_[CL * RS], sg[CL * RS];
   __shared__ float Aab[CL][CL + 1], Aak[CL][CL + 1], Brb[CL][CL + 1], Brk[CL][CL + 1],
-      Tm[CL][CL + 1], PU[CL][CL + 1], PY[CL][CL + 1];
+      Tm[CL][CL + 1];
   __shared__ float sv_[CL * RS];
   __shared__ float glv[KD];  // e^{G_L}: the chunk's total decay per key column
-  __shared__ float Wh[CL * RS];
+  // storage reused once its first tenant is dead (keeps the CTA small: 7 per SM):
+  float* Wh = sg;           // What, written in step 5; sg is last read in step 2
+  float(*PU)[CL + 1] = Aab;  // P_U, written in step 5; A_ab is last read in step 4
+  float(*PY)[CL + 1] = Brk;  // P_Y = B_rk + B_rb P_U, written in place over B_rk
   __shared__ int info[3];
   const int c = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
   if (tid == 0) {
