@@ -384,7 +384,8 @@ def side_measurements(model, w, dev, stream, step_bytes_of, hbm_gbs) -> dict:
 
 
 def continuous_batching(model, w, dev, stream, n_seqs: int, max_new: int, max_batch: int,
-                        world: int = 1, rank: int = 0, seed: int = 4) -> dict:
+                        world: int = 1, rank: int = 0, seed: int = 4,
+                        prefill_tokens: int = 16384) -> dict:
     """Config 4: n_seqs requests, prompt lengths ~U[16, 2048] and token ids uniform
     (seeded), max_new greedy tokens each, through ``ContinuousBatcher`` with decode
     batches of up to max_batch; sequences sharded over ranks by prompt length. Timed
@@ -402,7 +403,7 @@ def continuous_batching(model, w, dev, stream, n_seqs: int, max_new: int, max_ba
         warm.submit(Request(i, prompts[i][:64], 4))
     warm.run()
     del warm
-    b = ContinuousBatcher(eng, max_batch=max_batch, prefill_tokens=4096)
+    b = ContinuousBatcher(eng, max_batch=max_batch, prefill_tokens=prefill_tokens)
     for i in mine:
         b.submit(Request(i, prompts[i], max_new))
     torch.cuda.synchronize()
@@ -416,7 +417,8 @@ def continuous_batching(model, w, dev, stream, n_seqs: int, max_new: int, max_ba
     prompt_tok = sum(lens) if world > 1 else sum(lens[i] for i in mine)
     gen_tok = (n_seqs if world > 1 else len(mine)) * max_new
     return {"workload": f"{n_seqs} requests, prompts U[16,2048], {max_new} greedy tokens each, "
-                        f"decode batch <= {max_batch} per GPU", "seconds": sec,
+                        f"decode batch <= {max_batch} per GPU, prefill budget {prefill_tokens} tokens "
+                        f"per scheduler step", "seconds": sec,
             "tokens_per_s": (prompt_tok + gen_tok) / sec, "generated_tokens_per_s": gen_tok / sec,
             "prompt_tokens": prompt_tok, "generated_tokens": gen_tok, "scheduler_steps": b.steps}
 
