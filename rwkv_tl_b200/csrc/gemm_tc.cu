@@ -802,11 +802,25 @@ int gemm_tc_launch_persist(const rwkv7_gemm_problem* p, int n, int epi, cudaStre
 // Tile configuration and split-K by problem size. Large grids: 128 x 128 tiles,
 // 3 stages (two CTAs per SM). Small grids (batched decode): 128 x 64 tiles with 6
 // stages (144 KiB of operands in flight per CTA) and, when still fewer than 48
-// tiles, a K split with at least 8 K-blocks per slice. `ws` takes the split-K fp32
+// tiles, a K split with at least 4 K-blocks per slice and at most one wave of CTAs. `ws` takes the split-K fp32
 // partial tiles (ws_floats floats; no initial value needed). With `splits_out`
 // non-null the split-K reduce is left to the consumer: *splits_out receives the
 // number of K-slices parked in ws ([splits][M][N] fp32 per problem, problems back to
 // back), 1 when the GEMM wrote its output directly.
+// SM count of the current device (cached per device).
+static int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_t ws_floats,
                    cudaStream_t st, int* splits_out) {
   int tiles128 = 0, tiles64 = 0, min_kb = 1 << 30;
@@ -828,7 +842,9 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_
   }
   int splits = 1;
   if (ws && n4 && tiles64 < 48 && epi != EPI_ARGMAX) {
-    splits = max(1, min(min_kb / 8, (128 + tiles64 - 1) / tiles64));
+    // as many K-slices (of at least 4 K-blocks) as keep the grid within one wave of
+    // one CTA per SM: a second wave costs more than the slices save
+    splits = max(1, min(min_kb / 4, device_sm_count() / tiles64));
     while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
   }
   if (splits_out) *splits_out = splits;
