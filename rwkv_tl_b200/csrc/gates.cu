@@ -4,96 +4,185 @@
 // the padded rank buffer [M, 512] = v(32, zero-padded to 64) | tanh(w) hi, lo (64 + 64) | a(64) |
 // sigmoid(g) hi, lo (128 + 128) and the K-major weights w_lora_up_t [C, 512], giving v12, w12, a12,
 // g12 [M, C] (fp32 with decode rounding semantics, fp16 with prefill semantics).
-// This kernel finishes the gates.
+// This kernel finishes the gates. The planes (workspace, 256-byte aligned) move in
+// 16-byte accesses, 8 channels per lane.
 //
 // Reference: fused_gates (src/rwkv_tl/kernels/gates.py:182-213) and
 // fused_l2norm_neg_kk_a (src/rwkv_tl/kernels/dplr.py:45-71) on decode; the torch op
 // chain of demo/_rwkv7_base.py:242-260 on prefill.
-//
-// grid = (M, ceil(H / 8)), block = 256: warp w handles head 8 * blockIdx.y + w of
-// row blockIdx.x, lane l channels 2l, 2l+1 of the head.
 #include "common.cuh"
 
 namespace {
 constexpr float kSqrtE = 1.6487212707001282f;  // sqrt(e): w = exp(-sigmoid(.)/sqrt(e))
-
-template <typename T>
-__device__ __forceinline__ float2 ld2(const T* p);
-template <>
-__device__ __forceinline__ float2 ld2<float>(const float* p) {
-  return *reinterpret_cast<const float2*>(p);
-}
-template <>
-__device__ __forceinline__ float2 ld2<__half>(const __half* p) {
-  return __half22float2(*reinterpret_cast<const __half2*>(p));
-}
 }  // namespace
 
-template <int SEM, typename T>
-__global__ void __launch_bounds__(256) k_gates_ew(
+// N (2 or 8) consecutive channels of a workspace plane as floats.
+template <int N>
+__device__ __forceinline__ void ldn(const __half* p, float (&v)[N]) {
+  if constexpr (N == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
+    v[0] = f.x;
+    v[1] = f.y;
+  }
+}
+template <int N>
+__device__ __forceinline__ void ldn(const float* p, float (&v)[N]) {
+  if constexpr (N == 8) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    v[0] = a.x; v[1] = a.y;
+  }
+}
+// N channels of a per-layer weight vector (caller memory: 4-byte aligned loads).
+template <int N>
+__device__ __forceinline__ void ldw(const __half* p, float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    const float2 f = __half22float2(reinterpret_cast<const __half2*>(p)[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <int N>
+__device__ __forceinline__ void stn(__half* p, const float (&v)[N]) {
+  if constexpr (N == 8) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  } else {
+    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(v[0], v[1]);
+  }
+}
+
+// Per-head sum of squares with the summation tree of a 32-lane butterfly over
+// 2-channel partials (warp_sum: offsets 16 .. 1), so that every channel layout (and
+// the decode kernels, which sum that way) rounds identically. A lane holds P such
+// partials (old lanes P * lane .. P * lane + P - 1 of its head): butterfly offsets
+// >= P become shuffles between lanes, smaller ones adds within the lane.
+template <int P>
+__device__ __forceinline__ float head_sumsq(float (&p)[P]) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (off >= P) {
+#pragma unroll
+      for (int q = 0; q < P; ++q) p[q] += __shfl_xor_sync(0xffffffffu, p[q], off / P);
+    } else {
+      float t[P];
+#pragma unroll
+      for (int q = 0; q < P; ++q) t[q] = p[q] + p[q ^ off];
+#pragma unroll
+      for (int q = 0; q < P; ++q) p[q] = t[q];
+    }
+  }
+  return p[0];
+}
+
+// grid = (M, parts of a row), block = C / VPL lanes rounded up to a warp, at most
+// 256 per CTA. Each lane handles VPL consecutive channels (VPL = 8: 16-byte fp16
+// accesses, for large token batches; VPL = 2 for decode-size batches, more threads per
+// row); the 64 / VPL lanes of a head reduce its L2 norm together.
+template <int SEM, typename T, int VPL>
+__global__ void k_gates_ew(
     const T* __restrict__ lora,         // 4 x [M, C]: v12, w12, a12, g12
     const __half* __restrict__ rkv,     // 3 x [M, C]: r, k, v
     const __half* __restrict__ w0, const __half* __restrict__ a0, const __half* __restrict__ v0,
     const __half* __restrict__ k_k, const __half* __restrict__ k_a,
     __half* __restrict__ vfirst,        // [M, C] written on layer 0, read otherwise
     __half* __restrict__ gout,          // 6 x [M, C]: w, k, v, A, B, g
-    int M, int C, int H, int layer0) {
+    int M, int C, int layer0) {
   RWKV_GRID_DEP_ENTRY();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int m = blockIdx.x, h = blockIdx.y * 8 + warp;
-  if (h >= H) return;
+  constexpr int P = VPL / 2;
+  const int m = blockIdx.x;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * VPL;
+  const bool on = c < C;  // lanes past the row still join the group reduction
   const size_t plane = (size_t)M * C;
-  const int c = h * RWKV_HD + 2 * lane;
-  const size_t o = (size_t)m * C + c;
-  const float2 V12 = ld2<T>(lora + o), W12 = ld2<T>(lora + plane + o),
-               A12 = ld2<T>(lora + 2 * plane + o), G12 = ld2<T>(lora + 3 * plane + o);
-  const float2 kin = __half22float2(*reinterpret_cast<const __half2*>(rkv + plane + o));
-  const float2 vin = __half22float2(*reinterpret_cast<const __half2*>(rkv + 2 * plane + o));
-  float2 vf = vin;
-  if (layer0)
-    *reinterpret_cast<__half2*>(vfirst + o) = *reinterpret_cast<const __half2*>(rkv + 2 * plane + o);
-  else
-    vf = __half22float2(*reinterpret_cast<const __half2*>(vfirst + o));
-  const float2 W0 = __half22float2(*reinterpret_cast<const __half2*>(w0 + c));
-  const float2 A0 = __half22float2(*reinterpret_cast<const __half2*>(a0 + c));
-  const float2 V0 = __half22float2(*reinterpret_cast<const __half2*>(v0 + c));
-  const float2 KK = __half22float2(*reinterpret_cast<const __half2*>(k_k + c));
-  const float2 KA = __half22float2(*reinterpret_cast<const __half2*>(k_a + c));
-  const float v12[2] = {V12.x, V12.y}, w12[2] = {W12.x, W12.y}, a12[2] = {A12.x, A12.y},
-              g12[2] = {G12.x, G12.y}, kv[2] = {kin.x, kin.y}, vv[2] = {vin.x, vin.y},
-              vfv[2] = {vf.x, vf.y}, w0v[2] = {W0.x, W0.y}, a0v[2] = {A0.x, A0.y},
-              v0v[2] = {V0.x, V0.y}, kkv[2] = {KK.x, KK.y}, kav[2] = {KA.x, KA.y};
-  float wo[2], ko[2], vo[2], go[2], kk[2], a16[2];
-  float ss = 0.f;
+  const size_t o = (size_t)m * C + (on ? c : 0);
+  float ssq[P], kk[VPL], a16[VPL];
 #pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const float k = kv[e], v = vv[e];
-    if (SEM == SEM_DECODE) {
-      vo[e] = layer0 ? v : r16(v + sigmoidf_(v0v[e] + v12[e]) * (vfv[e] - v));
-      wo[e] = r16(expf(-sigmoidf_(w0v[e] + w12[e]) / kSqrtE));
-      const float a = sigmoidf_(a0v[e] + a12[e]);
-      a16[e] = r16(a);
-      kk[e] = r16(k * kkv[e]);
-      ko[e] = r16(k + kav[e] * (k * a - k));
-      go[e] = r16(g12[e]);
-      ss += kk[e] * kk[e];
+  for (int q = 0; q < P; ++q) ssq[q] = 0.f;
+  if (on) {
+    float x[VPL], y[VPL], kin[VPL], vin[VPL], vf[VPL], out[VPL];
+    ldn<VPL>(rkv + plane + o, kin);
+    ldn<VPL>(rkv + 2 * plane + o, vin);
+    if (layer0) {
+#pragma unroll
+      for (int e = 0; e < VPL; ++e) vf[e] = vin[e];
+      stn<VPL>(vfirst + o, vin);  // fp16 values round-trip exactly
     } else {
-      vo[e] = layer0 ? v : r16(v + r16(r16(sigmoidf_(r16(v0v[e] + v12[e]))) * r16(vfv[e] - v)));
-      wo[e] = r16(expf(r16(-r16(sigmoidf_(r16(w0v[e] + w12[e]))) / kSqrtE)));
-      const float a = r16(sigmoidf_(r16(a0v[e] + a12[e])));
-      a16[e] = a;
-      kk[e] = r16(k * kkv[e]);
-      ko[e] = r16(k + r16(kav[e] * r16(r16(k * a) - k)));
-      go[e] = r16(g12[e]);
-      ss += r16(kk[e] * kk[e]);
+      ldn<VPL>(vfirst + o, vf);
     }
+    // v
+    ldn<VPL>(lora + o, x);
+    ldw<VPL>(v0 + c, y);
+#pragma unroll
+    for (int e = 0; e < VPL; ++e) {
+      const float v = vin[e];
+      if (layer0)
+        out[e] = v;
+      else if (SEM == SEM_DECODE)
+        out[e] = r16(v + sigmoidf_(y[e] + x[e]) * (vf[e] - v));
+      else
+        out[e] = r16(v + r16(r16(sigmoidf_(r16(y[e] + x[e]))) * r16(vf[e] - v)));
+    }
+    stn<VPL>(gout + 2 * plane + o, out);
+    // w
+    ldn<VPL>(lora + plane + o, x);
+    ldw<VPL>(w0 + c, y);
+#pragma unroll
+    for (int e = 0; e < VPL; ++e)
+      out[e] = SEM == SEM_DECODE ? r16(expf(-sigmoidf_(y[e] + x[e]) / kSqrtE))
+                                 : r16(expf(r16(-r16(sigmoidf_(r16(y[e] + x[e]))) / kSqrtE)));
+    stn<VPL>(gout + o, out);
+    // a, k, k * k_k
+    ldn<VPL>(lora + 2 * plane + o, x);
+    ldw<VPL>(a0 + c, y);
+    float ka[VPL], kkv[VPL];
+    ldw<VPL>(k_a + c, ka);
+    ldw<VPL>(k_k + c, kkv);
+#pragma unroll
+    for (int e = 0; e < VPL; ++e) {
+      const float k = kin[e];
+      kk[e] = r16(k * kkv[e]);
+      if (SEM == SEM_DECODE) {
+        const float a = sigmoidf_(y[e] + x[e]);
+        a16[e] = r16(a);
+        out[e] = r16(k + ka[e] * (k * a - k));
+        ssq[e / 2] += kk[e] * kk[e];
+      } else {
+        const float a = r16(sigmoidf_(r16(y[e] + x[e])));
+        a16[e] = a;
+        out[e] = r16(k + r16(ka[e] * r16(r16(k * a) - k)));
+        ssq[e / 2] += r16(kk[e] * kk[e]);
+      }
+    }
+    stn<VPL>(gout + plane + o, out);
+    // g
+    ldn<VPL>(lora + 3 * plane + o, x);
+#pragma unroll
+    for (int e = 0; e < VPL; ++e) out[e] = r16(x[e]);
+    stn<VPL>(gout + 5 * plane + o, out);
   }
-  ss = warp_sum(ss);
-  float An[2], Bn[2];
+  const float ss = head_sumsq<P>(ssq);
+  if (!on) return;
+  float An[VPL], Bn[VPL];
   if (SEM == SEM_DECODE) {
     const float den = fmaxf(sqrtf(ss), 1e-12f);
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
+    for (int e = 0; e < VPL; ++e) {
       const float kn = kk[e] / den;
       An[e] = kn;
       Bn[e] = -(kn * a16[e]);
@@ -101,29 +190,32 @@ __global__ void __launch_bounds__(256) k_gates_ew(
   } else {
     const float den = fmaxf(r16(sqrtf(r16(ss))), 1e-12f);
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
+    for (int e = 0; e < VPL; ++e) {
       const float kn = r16(kk[e] / den);
       An[e] = kn;
       Bn[e] = -kn * a16[e];
     }
   }
-  *reinterpret_cast<__half2*>(gout + o) = __floats2half2_rn(wo[0], wo[1]);
-  *reinterpret_cast<__half2*>(gout + plane + o) = __floats2half2_rn(ko[0], ko[1]);
-  *reinterpret_cast<__half2*>(gout + 2 * plane + o) = __floats2half2_rn(vo[0], vo[1]);
-  *reinterpret_cast<__half2*>(gout + 3 * plane + o) = __floats2half2_rn(An[0], An[1]);
-  *reinterpret_cast<__half2*>(gout + 4 * plane + o) = __floats2half2_rn(Bn[0], Bn[1]);
-  *reinterpret_cast<__half2*>(gout + 5 * plane + o) = __floats2half2_rn(go[0], go[1]);
+  stn<VPL>(gout + 3 * plane + o, An);
+  stn<VPL>(gout + 4 * plane + o, Bn);
 }
 
 // `lora` is fp32 for decode semantics and fp16 for prefill semantics.
 int launch_gates_ew(int sem, const void* lora, const __half* rkv, const __half* w0,
                     const __half* a0, const __half* v0, const __half* k_k, const __half* k_a,
                     __half* vfirst, __half* gout, int M, int C, int layer0, cudaStream_t st) {
-  const int H = C / RWKV_HD;
-  dim3 grid(M, (H + 7) / 8);
-  if (sem == SEM_DECODE)
-    return rwkv_launch("gates_ew", k_gates_ew<SEM_DECODE, float>, grid, dim3(256), 0, st,
-                       (const float*)lora, rkv, w0, a0, v0, k_k, k_a, vfirst, gout, M, C, H, layer0);
-  return rwkv_launch("gates_ew", k_gates_ew<SEM_PREFILL, __half>, grid, dim3(256), 0, st,
-                     (const __half*)lora, rkv, w0, a0, v0, k_k, k_a, vfirst, gout, M, C, H, layer0);
+  const bool wide = M >= 1024;  // 8 channels per lane once the grid is large
+  const int lanes = ((C / (wide ? 8 : 2) + 31) / 32) * 32;
+  const int threads = lanes < 256 ? lanes : 256;
+  const dim3 grid(M, (lanes + threads - 1) / threads), block(threads);
+#define GATES_GO(S, T, V)                                                                      \
+  return rwkv_launch("gates_ew", k_gates_ew<S, T, V>, grid, block, 0, st, (const T*)lora, rkv, \
+                     w0, a0, v0, k_k, k_a, vfirst, gout, M, C, layer0)
+  if (sem == SEM_DECODE) {
+    if (wide) GATES_GO(SEM_DECODE, float, 8);
+    GATES_GO(SEM_DECODE, float, 2);
+  }
+  if (wide) GATES_GO(SEM_PREFILL, __half, 8);
+  GATES_GO(SEM_PREFILL, __half, 2);
+#undef GATES_GO
 }
