@@ -37,11 +37,14 @@ constexpr int RS = KD + 1;  // padded smem row stride (conflict-free column walk
 #ifndef PREP_MINB
 #define PREP_MINB 7
 #endif
-// Two-level scan: a sequence's chunks are cut into segments of SEG chunks (256 tokens).
+// Two-level scan: a sequence's chunks are cut into segments of SEG chunks (128 tokens).
 // Segments are scanned concurrently (the first from the true state, the others from
 // zero); each segment's transfer matrix Phi (product of its chunk maps) then carries
 // the true state across segments, and Q Phi corrects the later segments' outputs.
-constexpr int SEG = 16;
+#ifndef SEG_CHUNKS
+#define SEG_CHUNKS 8  // measured at T=4096: 8 beats 16 (0.5 %) and 32 (-5 %)
+#endif
+constexpr int SEG = SEG_CHUNKS;
 }  // namespace
 
 // chunk_cu[s] = chunks before sequence s, seg_cu[s] = segments (SEG chunks each) before
