@@ -248,8 +248,8 @@ template __global__ void k_wkv_tokens<SEM_PREFILL>(const __half*, const __half*,
 
 // One token per sequence (batched decode): grid = (n_seqs, H), 256 threads. All
 // state loads of a warp are issued together and no next-token buffer is kept, so the
-// kernel stays small enough for 6 CTAs per SM, 40 registers (enough bytes in flight to stream the
-// 2 x 16 KiB of state per (sequence, head) at HBM rate).
+// kernel fits 6 CTAs per SM at 40 registers: enough bytes in flight to stream the
+// 2 x 16 KiB of state per (sequence, head) at HBM rate.
 struct DecVecs {
   const __half *r, *w, *k, *v, *a, *b, *g;  // [n_seqs, C] each
 };
