@@ -347,9 +347,13 @@ constexpr int SCAN_ROWS = 32;                       // state rows per CTA
 constexpr int SCAN_THREADS = 256;                   // eight warps, four rows each
 constexpr int SLICE_F = SCAN_ROWS * RWS;            // per-CTA part of a record's row terms
 constexpr int STAGE_F = SHARED_F + SLICE_F;         // floats per ring stage
-// Chunk records in flight per CTA: a segment has at most SEG chunks and several
-// segment CTAs share an SM, so a short ring (47 KB, four CTAs per SM) suffices.
-constexpr int NSTAGE = 3;
+// Chunk records in flight per CTA: a segment has at most SEG chunks and three
+// segment CTAs share an SM, so a two-stage ring (50 KB) suffices; measured at
+// T=4096, two stages beat three (0.6 %: more of the SM's memory left to L1).
+#ifndef SCAN_NSTAGE
+#define SCAN_NSTAGE 2
+#endif
+constexpr int NSTAGE = SCAN_NSTAGE;
 constexpr size_t SCAN_SMEM = (size_t)NSTAGE * STAGE_F * sizeof(float) + 2 * NSTAGE * sizeof(uint64_t);
 static_assert((SHARED_F * 4) % 16 == 0 && (SLICE_F * 4) % 16 == 0 && (REC * 4) % 16 == 0,
               "bulk copies need 16-byte multiples");
@@ -674,7 +678,10 @@ static_assert(KD * PH_LD + 2 * CL * WQ_LD + 2 * CL * PH_LD + KD <= NSTAGE * STAG
 // blocks [0, n_phi) are (segment, head) transfer-matrix blocks (seg_phi_body, tensor
 // pipe), the rest are (segment, head, row group) scan blocks (chunk_scan_body, a
 // latency-bound chain); sharing the SMs, the first hide under the second.
-__global__ void __launch_bounds__(SCAN_THREADS, 3) k_scan_phi(
+#ifndef SCAN_MINB
+#define SCAN_MINB 3
+#endif
+__global__ void __launch_bounds__(SCAN_THREADS, SCAN_MINB) k_scan_phi(
     const float* __restrict__ rec, const int* __restrict__ cu, const int* __restrict__ chunk_cu,
     const int* __restrict__ seg_cu, const int* __restrict__ slots, float* __restrict__ rnn,
     __half* __restrict__ ybuf, float* __restrict__ yf32, float* __restrict__ lbuf,
