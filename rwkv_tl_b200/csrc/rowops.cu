@@ -8,32 +8,84 @@
 
 namespace {
 
-// LayerNorm of one row already in registers (4 channels per thread), fp32 math,
-// output rounded to fp16 like F.layer_norm on an fp16 tensor (weight.py:6-15).
-template <int NROW>
-__device__ __forceinline__ void ln_rows(float4 (&x)[NROW], const __half* w, const __half* b, int c,
-                                        int C, float* red) {
-  float s[NROW];
+// Block-wide sums of NV values per thread with the rounding of the layout of one
+// thread per 4 channels: a thread holds P partials (each the in-order sum over its 4
+// channels: the "4-channel threads" P * t .. P * t + P - 1). The 32-lane butterfly of
+// each 4-channel warp is replayed (offsets >= P as shuffles, smaller ones within the
+// thread), then the 4-channel warps' totals are added in order. blockDim.x * P must be
+// a multiple of 32.
+template <int P, int NV>
+__device__ __forceinline__ void block_sum_p(float (&v)[NV][P], float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (int)(blockDim.x * P + 31) >> 5;  // 4-channel warps
 #pragma unroll
-  for (int i = 0; i < NROW; ++i) s[i] = x[i].x + x[i].y + x[i].z + x[i].w;
-  block_sum<NROW>(s, red);
+  for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (off >= P) {
+#pragma unroll
+        for (int q = 0; q < P; ++q) v[i][q] += __shfl_xor_sync(0xffffffffu, v[i][q], off / P);
+      } else {
+        float t[P];
+#pragma unroll
+        for (int q = 0; q < P; ++q) t[q] = v[i][q] + v[i][q ^ off];
+#pragma unroll
+        for (int q = 0; q < P; ++q) v[i][q] = t[q];
+      }
+    }
+  }
+  __syncthreads();
+  if (((P * lane) & 31) == 0) {
+    const int w4 = (P * (32 * wid + lane)) >> 5;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) red[w4 * NV + i] = v[i][0];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float s = 0.f;
+    for (int w = 0; w < nw; ++w) s += red[w * NV + i];
+#pragma unroll
+    for (int q = 0; q < P; ++q) v[i][q] = s;
+  }
+  __syncthreads();
+}
+
+// LayerNorm of NROW rows already in registers (P groups of 4 channels per thread,
+// group q at channel c + 4q), fp32 math, output rounded to fp16 like F.layer_norm on
+// an fp16 tensor (weight.py:6-15).
+template <int NROW, int P>
+__device__ __forceinline__ void ln_rows(float4 (&x)[NROW][P], const __half* w, const __half* b,
+                                        int c, int C, float* red) {
+  float s[NROW][P];
+#pragma unroll
+  for (int i = 0; i < NROW; ++i)
+#pragma unroll
+    for (int q = 0; q < P; ++q) s[i][q] = x[i][q].x + x[i][q].y + x[i][q].z + x[i][q].w;
+  block_sum_p<P, NROW>(s, red);
   float mean[NROW];
 #pragma unroll
   for (int i = 0; i < NROW; ++i) {
-    mean[i] = s[i] / C;
-    const float dx = x[i].x - mean[i], dy = x[i].y - mean[i], dz = x[i].z - mean[i],
-                dw = x[i].w - mean[i];
-    s[i] = dx * dx + dy * dy + dz * dz + dw * dw;
-  }
-  block_sum<NROW>(s, red);
-  const float4 ww = load_h4(w + c), bb = load_h4(b + c);
+    mean[i] = s[i][0] / C;
 #pragma unroll
-  for (int i = 0; i < NROW; ++i) {
-    const float rstd = rsqrtf(s[i] / C + 1e-5f);
-    x[i].x = r16((x[i].x - mean[i]) * rstd * ww.x + bb.x);
-    x[i].y = r16((x[i].y - mean[i]) * rstd * ww.y + bb.y);
-    x[i].z = r16((x[i].z - mean[i]) * rstd * ww.z + bb.z);
-    x[i].w = r16((x[i].w - mean[i]) * rstd * ww.w + bb.w);
+    for (int q = 0; q < P; ++q) {
+      const float dx = x[i][q].x - mean[i], dy = x[i][q].y - mean[i], dz = x[i][q].z - mean[i],
+                  dw = x[i][q].w - mean[i];
+      s[i][q] = dx * dx + dy * dy + dz * dz + dw * dw;
+    }
+  }
+  block_sum_p<P, NROW>(s, red);
+#pragma unroll
+  for (int q = 0; q < P; ++q) {
+    const float4 ww = load_h4(w + c + 4 * q), bb = load_h4(b + c + 4 * q);
+#pragma unroll
+    for (int i = 0; i < NROW; ++i) {
+      const float rstd = rsqrtf(s[i][0] / C + 1e-5f);
+      x[i][q].x = r16((x[i][q].x - mean[i]) * rstd * ww.x + bb.x);
+      x[i][q].y = r16((x[i][q].y - mean[i]) * rstd * ww.y + bb.y);
+      x[i][q].z = r16((x[i][q].z - mean[i]) * rstd * ww.z + bb.z);
+      x[i][q].w = r16((x[i][q].w - mean[i]) * rstd * ww.w + bb.w);
+    }
   }
 }
 
@@ -68,11 +120,53 @@ __device__ __forceinline__ float4 pending_row4(const PendingResid& p, int m, int
 
 }  // namespace
 
+// P groups of 4 channels at p + 4q: one 16-byte access per thread for P = 2 (workspace
+// rows only: 16-byte aligned), 8-byte accesses otherwise.
+template <int P>
+__device__ __forceinline__ void load_rows(const __half* p, float4 (&v)[P]) {
+  if constexpr (P == 2) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), c = __half22float2(h[2]),
+                 d = __half22float2(h[3]);
+    v[0] = make_float4(a.x, a.y, b.x, b.y);
+    v[1] = make_float4(c.x, c.y, d.x, d.y);
+  } else {
+#pragma unroll
+    for (int q = 0; q < P; ++q) v[q] = load_h4(p + 4 * q);
+  }
+}
+template <int P>
+__device__ __forceinline__ void store_rows(__half* p, const float4 (&v)[P]) {
+  if constexpr (P == 2) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+    h[0] = __floats2half2_rn(v[0].x, v[0].y);
+    h[1] = __floats2half2_rn(v[0].z, v[0].w);
+    h[2] = __floats2half2_rn(v[1].x, v[1].y);
+    h[3] = __floats2half2_rn(v[1].z, v[1].w);
+    *reinterpret_cast<uint4*>(p) = u;
+  } else {
+#pragma unroll
+    for (int q = 0; q < P; ++q) store_h4(p + 4 * q, v[q]);
+  }
+}
+// Caller memory (embedding rows, state x, mix vectors): 8-byte accesses.
+template <int P>
+__device__ __forceinline__ void load_user(const __half* p, float4 (&v)[P]) {
+#pragma unroll
+  for (int q = 0; q < P; ++q) v[q] = load_h4(p + 4 * q);
+}
+
+// Row kernels: one CTA per token row, C / (4P) threads, 4P channels per thread (P = 1
+// for small batches, P = 2 -- 16-byte accesses, twice the rows in flight per SM -- for
+// large ones); LayerNorm sums round the same for both.
+
 // TMIX input stage: [embedding gather] + LN1 + token shift + 6 lerps.
 //   x      : [M, C] layer input (written here when `tokens` != NULL: layer 0 gathers emb rows)
 //   xmix   : 6 x [M, C] = xr, xw, xk, xv, xa, xg
 //   xlast  : [S, C] LN1 output of each sequence's last row (new state x)
-template <int SEM>
+template <int SEM, int P>
 __global__ void k_tmix_rows(__half* __restrict__ x, const int64_t* __restrict__ tokens,
                             const __half* __restrict__ emb, const __half* __restrict__ ln_w,
                             const __half* __restrict__ ln_b, const __half* __restrict__ mix6,
@@ -82,34 +176,51 @@ __global__ void k_tmix_rows(__half* __restrict__ x, const int64_t* __restrict__ 
                             const PendingResid pend) {
   RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32 * 2];
-  const int m = blockIdx.x, c = threadIdx.x * 4;
+  const int m = blockIdx.x, c = threadIdx.x * 4 * P;
   const int s = row_seq[m];
   const bool first = (m == cu[s]), last = (m == cu[s + 1] - 1);
-  float4 v[2];
+  float4 v[2][P];
   if (tokens) {
-    v[0] = load_h4(emb + (size_t)tokens[m] * C + c);
-    v[1] = first ? v[0] : load_h4(emb + (size_t)tokens[m - 1] * C + c);
-    store_h4(x + (size_t)m * C + c, v[0]);
+    load_user<P>(emb + (size_t)tokens[m] * C + c, v[0]);
+    if (!first) load_user<P>(emb + (size_t)tokens[m - 1] * C + c, v[1]);
+    store_rows<P>(x + (size_t)m * C + c, v[0]);
   } else if (pend.ws) {  // x = res + (split-K GEMM output), finished here
-    v[0] = pending_row4(pend, m, c, M, C);
-    v[1] = first ? v[0] : pending_row4(pend, m - 1, c, M, C);
-    store_h4(x + (size_t)m * C + c, v[0]);
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      v[0][q] = pending_row4(pend, m, c + 4 * q, M, C);
+      if (!first) v[1][q] = pending_row4(pend, m - 1, c + 4 * q, M, C);
+    }
+    store_rows<P>(x + (size_t)m * C + c, v[0]);
   } else {
-    v[0] = load_h4(x + (size_t)m * C + c);
-    v[1] = first ? v[0] : load_h4(x + (size_t)(m - 1) * C + c);
+    load_rows<P>(x + (size_t)m * C + c, v[0]);
+    if (!first) load_rows<P>(x + (size_t)(m - 1) * C + c, v[1]);
   }
-  ln_rows<2>(v, ln_w, ln_b, c, C, red);
+  if (first) {
+#pragma unroll
+    for (int q = 0; q < P; ++q) v[1][q] = v[0][q];
+  }
+  ln_rows<2, P>(v, ln_w, ln_b, c, C, red);
   const int slot = slots ? slots[s] : s;
-  const float4 prev = first ? load_h4(state_x + (size_t)slot * C + c) : v[1];
+  float4 prev[P];
+  if (first)
+    load_user<P>(state_x + (size_t)slot * C + c, prev);
+  else
+#pragma unroll
+    for (int q = 0; q < P; ++q) prev[q] = v[1][q];
   const size_t plane = (size_t)M * C;
 #pragma unroll
-  for (int j = 0; j < 6; ++j)
-    store_h4(xmix + j * plane + (size_t)m * C + c, lerp4<SEM>(v[0], prev, load_h4(mix6 + j * C + c)));
-  if (last) store_h4(xlast + (size_t)s * C + c, v[0]);
+  for (int j = 0; j < 6; ++j) {
+    float4 mu[P], o[P];
+    load_user<P>(mix6 + j * C + c, mu);
+#pragma unroll
+    for (int q = 0; q < P; ++q) o[q] = lerp4<SEM>(v[0][q], prev[q], mu[q]);
+    store_rows<P>(xmix + j * plane + (size_t)m * C + c, o);
+  }
+  if (last) store_rows<P>(xlast + (size_t)s * C + c, v[0]);
 }
 
 // CMIX input stage: LN2 + token shift + one lerp (x_k).
-template <int SEM>
+template <int SEM, int P>
 __global__ void k_cmix_rows(__half* __restrict__ x, const __half* __restrict__ ln_w,
                             const __half* __restrict__ ln_b, const __half* __restrict__ mu,
                             const __half* __restrict__ state_x, const int* __restrict__ row_seq,
@@ -118,23 +229,38 @@ __global__ void k_cmix_rows(__half* __restrict__ x, const __half* __restrict__ l
                             const PendingResid pend) {
   RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32 * 2];
-  const int m = blockIdx.x, c = threadIdx.x * 4;
+  const int m = blockIdx.x, c = threadIdx.x * 4 * P;
   const int s = row_seq[m];
   const bool first = (m == cu[s]), last = (m == cu[s + 1] - 1);
-  float4 v[2];
+  float4 v[2][P];
   if (pend.ws) {  // x = res + (split-K GEMM output), finished here
-    v[0] = pending_row4(pend, m, c, M, C);
-    v[1] = first ? v[0] : pending_row4(pend, m - 1, c, M, C);
-    store_h4(x + (size_t)m * C + c, v[0]);
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      v[0][q] = pending_row4(pend, m, c + 4 * q, M, C);
+      if (!first) v[1][q] = pending_row4(pend, m - 1, c + 4 * q, M, C);
+    }
+    store_rows<P>(x + (size_t)m * C + c, v[0]);
   } else {
-    v[0] = load_h4(x + (size_t)m * C + c);
-    v[1] = first ? v[0] : load_h4(x + (size_t)(m - 1) * C + c);
+    load_rows<P>(x + (size_t)m * C + c, v[0]);
+    if (!first) load_rows<P>(x + (size_t)(m - 1) * C + c, v[1]);
   }
-  ln_rows<2>(v, ln_w, ln_b, c, C, red);
+  if (first) {
+#pragma unroll
+    for (int q = 0; q < P; ++q) v[1][q] = v[0][q];
+  }
+  ln_rows<2, P>(v, ln_w, ln_b, c, C, red);
   const int slot = slots ? slots[s] : s;
-  const float4 prev = first ? load_h4(state_x + (size_t)slot * C + c) : v[1];
-  store_h4(xk + (size_t)m * C + c, lerp4<SEM>(v[0], prev, load_h4(mu + c)));
-  if (last) store_h4(xlast + (size_t)s * C + c, v[0]);
+  float4 prev[P], mv[P], o[P];
+  if (first)
+    load_user<P>(state_x + (size_t)slot * C + c, prev);
+  else
+#pragma unroll
+    for (int q = 0; q < P; ++q) prev[q] = v[1][q];
+  load_user<P>(mu + c, mv);
+#pragma unroll
+  for (int q = 0; q < P; ++q) o[q] = lerp4<SEM>(v[0][q], prev[q], mv[q]);
+  store_rows<P>(xk + (size_t)m * C + c, o);
+  if (last) store_rows<P>(xlast + (size_t)s * C + c, v[0]);
 }
 
 // ln_out of the rows that produce logits: out[i] = LN(x[rows[i]]).
@@ -144,10 +270,10 @@ __global__ void k_ln_rows(const __half* __restrict__ x, const int* __restrict__ 
   RWKV_GRID_DEP_ENTRY();
   __shared__ float red[32];
   const int i = blockIdx.x, c = threadIdx.x * 4;
-  float4 v[1];
-  v[0] = pend.ws ? pending_row4(pend, rows[i], c, M, C) : load_h4(x + (size_t)rows[i] * C + c);
-  ln_rows<1>(v, w, b, c, C, red);
-  store_h4(out + (size_t)i * C + c, v[0]);
+  float4 v[1][1];
+  v[0][0] = pend.ws ? pending_row4(pend, rows[i], c, M, C) : load_h4(x + (size_t)rows[i] * C + c);
+  ln_rows<1, 1>(v, w, b, c, C, red);
+  store_h4(out + (size_t)i * C + c, v[0][0]);
 }
 
 // Greedy ids from the head GEMM's per-row keys (EPI_ARGMAX).
@@ -172,23 +298,41 @@ __global__ void k_scatter_state_x(const __half* __restrict__ xlast, __half* __re
   *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
 }
 
+// 8 channels per thread once the batch is large (and C / 8 is whole warps).
+static bool rows_wide(int M, int C) { return M >= 1024 && C % 256 == 0; }
+
 int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* emb,
                      const __half* ln_w, const __half* ln_b, const __half* mix6,
                      const __half* state_x, const int* row_seq, const int* cu, const int* slots,
                      __half* xmix, __half* xlast, int M, int C, PendingResid pend,
                      cudaStream_t st) {
-  return rwkv_launch("tmix_rows", sem == SEM_DECODE ? k_tmix_rows<SEM_DECODE> : k_tmix_rows<SEM_PREFILL>,
-                     dim3(M), dim3(C / 4), 0, st, x, tokens, emb, ln_w, ln_b, mix6, state_x, row_seq,
-                     cu, slots, xmix, xlast, M, C, pend);
+#define TMIX_GO(S, P)                                                                          \
+  return rwkv_launch("tmix_rows", k_tmix_rows<S, P>, dim3(M), dim3(C / (4 * P)), 0, st, x,     \
+                     tokens, emb, ln_w, ln_b, mix6, state_x, row_seq, cu, slots, xmix, xlast, M, \
+                     C, pend)
+  if (rows_wide(M, C)) {
+    if (sem == SEM_DECODE) TMIX_GO(SEM_DECODE, 2);
+    TMIX_GO(SEM_PREFILL, 2);
+  }
+  if (sem == SEM_DECODE) TMIX_GO(SEM_DECODE, 1);
+  TMIX_GO(SEM_PREFILL, 1);
+#undef TMIX_GO
 }
 
 int launch_cmix_rows(int sem, __half* x, const __half* ln_w, const __half* ln_b,
                      const __half* mu, const __half* state_x, const int* row_seq, const int* cu,
                      const int* slots, __half* xk, __half* xlast, int M, int C, PendingResid pend,
                      cudaStream_t st) {
-  return rwkv_launch("cmix_rows", sem == SEM_DECODE ? k_cmix_rows<SEM_DECODE> : k_cmix_rows<SEM_PREFILL>,
-                     dim3(M), dim3(C / 4), 0, st, x, ln_w, ln_b, mu, state_x, row_seq, cu, slots, xk,
-                     xlast, M, C, pend);
+#define CMIX_GO(S, P)                                                                          \
+  return rwkv_launch("cmix_rows", k_cmix_rows<S, P>, dim3(M), dim3(C / (4 * P)), 0, st, x,     \
+                     ln_w, ln_b, mu, state_x, row_seq, cu, slots, xk, xlast, M, C, pend)
+  if (rows_wide(M, C)) {
+    if (sem == SEM_DECODE) CMIX_GO(SEM_DECODE, 2);
+    CMIX_GO(SEM_PREFILL, 2);
+  }
+  if (sem == SEM_DECODE) CMIX_GO(SEM_DECODE, 1);
+  CMIX_GO(SEM_PREFILL, 1);
+#undef CMIX_GO
 }
 
 int launch_ln_rows(const __half* x, const int* rows, const __half* w, const __half* b,

@@ -31,7 +31,13 @@ def test_continuous_batching_matches_sequential_generate():
     for r in reqs:
         ref, _ = m.generate(r.prompt.to(dev), State(w.L, w.C, 64, device=dev), r.max_new_tokens)
         assert len(r.output) == r.max_new_tokens
-        assert r.output[0] == ref[0], r.rid  # same state -> same first greedy token
+        if r.output[0] != ref[0]:
+            # same state -> same first greedy token, up to a near-tie: small-batch decode sums
+            # with float atomics, so its last fp32 bits vary from run to run
+            lg, _ = m.forward(r.prompt.to(dev), State(w.L, w.C, 64, device=dev))
+            lg = lg.float()
+            gap = abs(float(lg[ref[0]] - lg[r.output[0]]))
+            assert gap <= 2e-3 * float(lg.abs().max()), (r.rid, gap)
         agree += sum(a == c for a, c in zip(r.output, ref))
         total += len(ref)
     # prefill split at other chunk boundaries rounds differently in fp32; a near-tie
