@@ -26,6 +26,29 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// warp_sum for a layout in which one lane does the work of P lanes: lane j holds the
+// P partials of "lanes" P * j .. P * j + P - 1, and a group of 32 / P lanes stands for
+// one warp. Replays warp_sum's butterfly (offsets >= P as shuffles by offset / P,
+// smaller ones as adds within the lane), so the result rounds exactly like warp_sum
+// over the 32 original partials. P = 1 is warp_sum itself.
+template <int P>
+__device__ __forceinline__ float warp_sum_p(float (&p)[P]) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (off >= P) {
+#pragma unroll
+      for (int q = 0; q < P; ++q) p[q] += __shfl_xor_sync(0xffffffffu, p[q], off / P);
+    } else {
+      float t[P];
+#pragma unroll
+      for (int q = 0; q < P; ++q) t[q] = p[q] + p[q ^ off];
+#pragma unroll
+      for (int q = 0; q < P; ++q) p[q] = t[q];
+    }
+  }
+  return p[0];
+}
+
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 // 4 x fp16 <-> float4 through one 8-byte access.

@@ -68,29 +68,6 @@ __device__ __forceinline__ void stn(__half* p, const float (&v)[N]) {
   }
 }
 
-// Per-head sum of squares with the summation tree of a 32-lane butterfly over
-// 2-channel partials (warp_sum: offsets 16 .. 1), so that every channel layout (and
-// the decode kernels, which sum that way) rounds identically. A lane holds P such
-// partials (old lanes P * lane .. P * lane + P - 1 of its head): butterfly offsets
-// >= P become shuffles between lanes, smaller ones adds within the lane.
-template <int P>
-__device__ __forceinline__ float head_sumsq(float (&p)[P]) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    if (off >= P) {
-#pragma unroll
-      for (int q = 0; q < P; ++q) p[q] += __shfl_xor_sync(0xffffffffu, p[q], off / P);
-    } else {
-      float t[P];
-#pragma unroll
-      for (int q = 0; q < P; ++q) t[q] = p[q] + p[q ^ off];
-#pragma unroll
-      for (int q = 0; q < P; ++q) p[q] = t[q];
-    }
-  }
-  return p[0];
-}
-
 // grid = (M, parts of a row), block = C / VPL lanes rounded up to a warp, at most
 // 256 per CTA. Each lane handles VPL consecutive channels (VPL = 8: 16-byte fp16
 // accesses, for large token batches; VPL = 2 for decode-size batches, more threads per
@@ -176,7 +153,7 @@ __global__ void k_gates_ew(
     for (int e = 0; e < VPL; ++e) out[e] = r16(x[e]);
     stn<VPL>(gout + 5 * plane + o, out);
   }
-  const float ss = head_sumsq<P>(ssq);
+  const float ss = warp_sum_p<P>(ssq);
   if (!on) return;
   float An[VPL], Bn[VPL];
   if (SEM == SEM_DECODE) {

@@ -825,48 +825,107 @@ __global__ void __launch_bounds__(256) k_seg_fix(const int* __restrict__ cu,
   }
 }
 
-// Per-head GroupNorm + bonus + g gate on precomputed y (one warp per head and row).
-// grid = M rows, block = C / 2 threads.
-template <int SEM>
+namespace {
+// V consecutive fp16 channels (V = 2: 4-byte, V = 8: 16-byte access) as floats.
+template <int V>
+__device__ __forceinline__ void ld_ch(const __half* p, float (&v)[V]) {
+  if constexpr (V == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
+    v[0] = f.x;
+    v[1] = f.y;
+  }
+}
+// Caller vectors (r_k, ln_x weights): 4-byte loads whatever V.
+template <int V>
+__device__ __forceinline__ void ld_ch_user(const __half* p, float (&v)[V]) {
+#pragma unroll
+  for (int i = 0; i < V / 2; ++i) {
+    const float2 f = __half22float2(reinterpret_cast<const __half2*>(p)[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+}  // namespace
+
+// Per-head GroupNorm + bonus + g gate on precomputed y. grid = M rows, block = C / V
+// threads, V channels per thread: V = 2 (one warp per head) or, for large batches, V = 8
+// (8 lanes per head, 16-byte accesses); the head sums replay warp_sum's tree
+// (warp_sum_p), so both round identically.
+template <int SEM, int V>
 __global__ void k_wkv_epilogue(const __half* __restrict__ ybuf, const __half* __restrict__ rbuf,
                                const __half* __restrict__ gbuf, size_t plane,
                                const __half* __restrict__ r_k, const __half* __restrict__ lnx_w,
                                const __half* __restrict__ lnx_b, __half* __restrict__ yg, int C) {
   RWKV_GRID_DEP_ENTRY();
-  const int m = blockIdx.x, c = threadIdx.x * 2;
+  constexpr int P = V / 2;
+  const int m = blockIdx.x, c = threadIdx.x * V;
   const size_t o = (size_t)m * C + c;
-  const float2 y = __half22float2(*reinterpret_cast<const __half2*>(ybuf + o));
-  const float mean = warp_sum(y.x + y.y) * (1.0f / RWKV_HD);
-  const float dx = y.x - mean, dy = y.y - mean;
-  const float var = warp_sum(dx * dx + dy * dy) * (1.0f / RWKV_HD);
+  float y[V], rr[V], kk[V], vv[V], gg[V], rk[V], lw[V], lb[V], p[P];
+  ld_ch<V>(ybuf + o, y);
+#pragma unroll
+  for (int q = 0; q < P; ++q) p[q] = y[2 * q] + y[2 * q + 1];
+  const float mean = warp_sum_p<P>(p) * (1.0f / RWKV_HD);
+  float d[V];
+#pragma unroll
+  for (int e = 0; e < V; ++e) d[e] = y[e] - mean;
+#pragma unroll
+  for (int q = 0; q < P; ++q) p[q] = d[2 * q] * d[2 * q] + d[2 * q + 1] * d[2 * q + 1];
+  const float var = warp_sum_p<P>(p) * (1.0f / RWKV_HD);
   const float rstd = 1.0f / sqrtf(var + 64e-5f);
-  const float2 rr = __half22float2(*reinterpret_cast<const __half2*>(rbuf + o));
-  const float2 kk = __half22float2(*reinterpret_cast<const __half2*>(gbuf + plane + o));
-  const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(gbuf + 2 * plane + o));
-  const float2 gg = __half22float2(*reinterpret_cast<const __half2*>(gbuf + 5 * plane + o));
-  const float2 rk = __half22float2(*reinterpret_cast<const __half2*>(r_k + c));
-  const float2 lw = __half22float2(*reinterpret_cast<const __half2*>(lnx_w + c));
-  const float2 lb = __half22float2(*reinterpret_cast<const __half2*>(lnx_b + c));
-  float ox, oy;
+  ld_ch<V>(rbuf + o, rr);
+  ld_ch<V>(gbuf + plane + o, kk);
+  ld_ch<V>(gbuf + 2 * plane + o, vv);
+  ld_ch<V>(gbuf + 5 * plane + o, gg);
+  ld_ch_user<V>(r_k + c, rk);
+  ld_ch_user<V>(lnx_w + c, lw);
+  ld_ch_user<V>(lnx_b + c, lb);
+  float out[V];
   if (SEM == SEM_DECODE) {
-    float p = rr.x * kk.x * rk.x;
-    p += rr.y * kk.y * rk.y;
-    const float rkrk = warp_sum(p);
-    ox = r16(dx * rstd * lw.x + lb.x + rkrk * vv.x);
-    oy = r16(dy * rstd * lw.y + lb.y + rkrk * vv.y);
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      p[q] = rr[2 * q] * kk[2 * q] * rk[2 * q];
+      p[q] += rr[2 * q + 1] * kk[2 * q + 1] * rk[2 * q + 1];
+    }
+    const float rkrk = warp_sum_p<P>(p);
+#pragma unroll
+    for (int e = 0; e < V; ++e) out[e] = r16(d[e] * rstd * lw[e] + lb[e] + rkrk * vv[e]);
   } else {
-    const float fx = r16(dx * rstd * lw.x + lb.x), fy = r16(dy * rstd * lw.y + lb.y);
-    const float rkrk = r16(warp_sum(r16(r16(rr.x * kk.x) * rk.x) + r16(r16(rr.y * kk.y) * rk.y)));
-    ox = r16(fx + r16(rkrk * vv.x));
-    oy = r16(fy + r16(rkrk * vv.y));
+#pragma unroll
+    for (int q = 0; q < P; ++q)
+      p[q] = r16(r16(rr[2 * q] * kk[2 * q]) * rk[2 * q]) +
+             r16(r16(rr[2 * q + 1] * kk[2 * q + 1]) * rk[2 * q + 1]);
+    const float rkrk = r16(warp_sum_p<P>(p));
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const float f = r16(d[e] * rstd * lw[e] + lb[e]);
+      out[e] = r16(f + r16(rkrk * vv[e]));
+    }
   }
-  *reinterpret_cast<__half2*>(yg + o) = __floats2half2_rn(ox * gg.x, oy * gg.y);
+  if constexpr (V == 8) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      h[i] = __floats2half2_rn(out[2 * i] * gg[2 * i], out[2 * i + 1] * gg[2 * i + 1]);
+    *reinterpret_cast<uint4*>(yg + o) = u;
+  } else {
+    *reinterpret_cast<__half2*>(yg + o) = __floats2half2_rn(out[0] * gg[0], out[1] * gg[1]);
+  }
 }
 
 // Scratch of the chunked recurrence (floats, in this order): chunk records [chunks][H][REC],
 // Q Phi per chunk [chunks][H][16 x 64], per segment the zero-start end state, the
 // transfer Phi and the true start state [segments][H][64 x 64] each, fp32 outputs
-// [M][C], then the segment table (S + 1 ints). chunks <= M/16 + S, segments <= M/256 + S.
+// [M][C], then the segment table (S + 1 ints). chunks <= M/16 + S, segments <= M/(16 SEG) + S.
 struct ChunkScratch {
   float *rec, *qt, *lbuf, *phi, *sst, *yf32;
   int* seg_cu;
@@ -949,8 +1008,18 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
 int launch_wkv_epilogue(int sem, const __half* ybuf, const __half* rbuf, const __half* gbuf,
                         size_t plane, const __half* r_k, const __half* lnx_w,
                         const __half* lnx_b, __half* yg, int M, int C, cudaStream_t st) {
-  return rwkv_launch("wkv_epilogue", sem == SEM_DECODE ? k_wkv_epilogue<SEM_DECODE> : k_wkv_epilogue<SEM_PREFILL>,
-                     dim3(M), dim3(C / 2), 0, st, ybuf, rbuf, gbuf, plane, r_k, lnx_w, lnx_b, yg, C);
+  // 8 channels per thread on large batches (C / 8 whole warps)
+  const bool wide = M >= 1024 && C % 256 == 0;
+#define EPI_GO(S, V)                                                                           \
+  return rwkv_launch("wkv_epilogue", k_wkv_epilogue<S, V>, dim3(M), dim3(C / V), 0, st, ybuf, \
+                     rbuf, gbuf, plane, r_k, lnx_w, lnx_b, yg, C)
+  if (wide) {
+    if (sem == SEM_DECODE) EPI_GO(SEM_DECODE, 8);
+    EPI_GO(SEM_PREFILL, 8);
+  }
+  if (sem == SEM_DECODE) EPI_GO(SEM_DECODE, 2);
+  EPI_GO(SEM_PREFILL, 2);
+#undef EPI_GO
 }
 
 __global__ void k_uniform_cu(int* cu, int S, int T) {

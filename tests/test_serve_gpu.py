@@ -1,6 +1,6 @@
 """Continuous batching on the real model: requests admitted into 4 slots, prompts
 prefilled in 48-token varlen chunks across steps, decode batches of 1..4 sequences,
-against running each request alone through ``generate`` (greedy)."""
+against running each request alone through the sequential model (greedy)."""
 
 from __future__ import annotations
 
@@ -27,22 +27,18 @@ def test_continuous_batching_matches_sequential_generate():
         b.submit(r)
     done = b.run()
     assert sorted(r.rid for r in done) == list(range(len(reqs)))
-    agree = total = 0
+    # Teacher-forced against the sequential model: every token the batcher chose must be
+    # the sequential greedy choice up to a near-tie. (Comparing free-running continuations
+    # is fragile: small-batch decode sums with float atomics, its last fp32 bits vary from
+    # run to run, and with random weights a flipped near-tie changes the whole tail.)
     for r in reqs:
-        ref, _ = m.generate(r.prompt.to(dev), State(w.L, w.C, 64, device=dev), r.max_new_tokens)
         assert len(r.output) == r.max_new_tokens
-        if r.output[0] != ref[0]:
-            # same state -> same first greedy token, up to a near-tie: small-batch decode sums
-            # with float atomics, so its last fp32 bits vary from run to run
-            lg, _ = m.forward(r.prompt.to(dev), State(w.L, w.C, 64, device=dev))
+        lg, S = m.forward(r.prompt.to(dev), State(w.L, w.C, 64, device=dev))
+        for i, t in enumerate(r.output):
             lg = lg.float()
-            gap = abs(float(lg[ref[0]] - lg[r.output[0]]))
-            assert gap <= 2e-3 * float(lg.abs().max()), (r.rid, gap)
-        agree += sum(a == c for a, c in zip(r.output, ref))
-        total += len(ref)
-    # prefill split at other chunk boundaries rounds differently in fp32; a near-tie
-    # can flip one greedy id, after which the two continuations differ
-    assert agree >= 0.9 * total, (agree, total)
+            gap = float(lg.max() - lg[t])
+            assert gap <= 5e-3 * float(lg.abs().max()), (r.rid, i, gap)
+            lg, S = m.decode(torch.tensor(t, device=dev), S)
     from rwkv_tl_b200 import _lib
 
     assert _lib.load().rwkv_b200_device_error() == 0
