@@ -33,7 +33,10 @@ constexpr int REC = SHARED_F + KD * RWS;      // floats per (chunk, head) record
 // with U = sum_j v_j Kt_j, the whole value input of the chunk to that state row.
 constexpr int OFF_W = 0, OFF_Q = CL * KD, OFF_B = 2 * CL * KD, OFF_G = 3 * CL * KD,
               OFF_RW = SHARED_F;
-constexpr int RS = KD + 1;  // padded smem row stride (conflict-free column walks)
+// Shared-memory row strides of the chunk prep. Rows read along k or by broadcast use
+// KD (float4 rows); sb_ / sk_, which 16 threads read at 16 different rows at once, use
+// KD + 4 so that a quarter-warp's float4 loads fall in distinct banks.
+constexpr int RSA = KD, RSB = KD + 4;
 #ifndef PREP_MINB
 #define PREP_MINB 7
 #endif
@@ -105,11 +108,12 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
     const int* __restrict__ cu,
     const int* __restrict__ chunk_cu, int S, int C, int M, float* __restrict__ rec) {
   RWKV_GRID_DEP_ENTRY();
-  __shared__ float sa_[CL * RS], sb_[CL * RS], sk_[CL * RS], sr_[CL * RS], sg[CL * RS];
+  __shared__ __align__(16) float sa_[CL * RSA], sb_[CL * RSB], sk_[CL * RSB], sr_[CL * RSA],
+      sg[CL * RSA];
   __shared__ float Aab[CL][CL + 1], Aak[CL][CL + 1], Brb[CL][CL + 1], Brk[CL][CL + 1],
       Tm[CL][CL + 1];
-  __shared__ float sv_[CL * RS];
-  __shared__ float glv[KD];  // e^{G_L}: the chunk's total decay per key column
+  __shared__ __align__(16) float sv_[CL * RSA];
+  __shared__ __align__(16) float glv[KD];  // e^{G_L}: the chunk's total decay per key column
   // storage reused once its first tenant is dead (keeps the CTA small: 7 per SM):
   float* Wh = sg;           // What, written in step 5; sg is last read in step 2
   float(*PU)[CL + 1] = Aab;  // P_U, written in step 5; A_ab is last read in step 4
@@ -147,26 +151,26 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
       auto ld = [&](const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p + o)); };
       r = ld(rb); w = ld(wb); kk = ld(kb); vv = ld(vb); a = ld(ab); b = ld(bb);
     }
-    const int q = t * RS + k;
+    const int q = t * RSA + k, qb = t * RSB + k;
     sv_[q] = vv.x; sv_[q + 1] = vv.y;
     sr_[q] = r.x; sr_[q + 1] = r.y;
     sg[q] = logf(w.x); sg[q + 1] = logf(w.y);
-    sk_[q] = kk.x; sk_[q + 1] = kk.y;
+    sk_[qb] = kk.x; sk_[qb + 1] = kk.y;
     sa_[q] = a.x; sa_[q + 1] = a.y;
-    sb_[q] = b.x; sb_[q + 1] = b.y;
+    sb_[qb] = b.x; sb_[qb + 1] = b.y;
   }
   __syncthreads();
   // 2. cumulative log decay per column, then decay-scaled vectors
   if (tid < KD) {
     float g = 0.f, egp = 1.f;  // e^{G_{t-1}}, carried
     for (int t = 0; t < CL; ++t) {
-      g += sg[t * RS + tid];
+      g += sg[t * RSA + tid];
       const float eg = expf(g), egi = 1.0f / eg;
-      sa_[t * RS + tid] *= egp;
-      sb_[t * RS + tid] *= egi;
-      sk_[t * RS + tid] *= egi;
-      sr_[t * RS + tid] *= eg;
-      sg[t * RS + tid] = g;
+      sa_[t * RSA + tid] *= egp;
+      sb_[t * RSB + tid] *= egi;
+      sk_[t * RSB + tid] *= egi;
+      sr_[t * RSA + tid] *= eg;
+      sg[t * RSA + tid] = g;
       egp = eg;
     }
     glv[tid] = expf(g);
@@ -177,10 +181,17 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
     const int t = tid >> 4, j = tid & 15;
     float aab = 0.f, aak = 0.f, brb = 0.f, brk = 0.f;
     if (j <= t) {
-      for (int k = 0; k < KD; ++k) {
-        const float at = sa_[t * RS + k], rt = sr_[t * RS + k];
-        const float bh = sb_[j * RS + k], kh = sk_[j * RS + k];
-        aab += at * bh; aak += at * kh; brb += rt * bh; brk += rt * kh;
+      // float4 rows, each sum still taken in k order
+      const float4* A4 = reinterpret_cast<const float4*>(sa_ + t * RSA);
+      const float4* R4 = reinterpret_cast<const float4*>(sr_ + t * RSA);
+      const float4* B4 = reinterpret_cast<const float4*>(sb_ + j * RSB);
+      const float4* K4 = reinterpret_cast<const float4*>(sk_ + j * RSB);
+      for (int k4 = 0; k4 < KD / 4; ++k4) {
+        const float4 at = A4[k4], rt = R4[k4], bh = B4[k4], kh = K4[k4];
+        aab += at.x * bh.x; aak += at.x * kh.x; brb += rt.x * bh.x; brk += rt.x * kh.x;
+        aab += at.y * bh.y; aak += at.y * kh.y; brb += rt.y * bh.y; brk += rt.y * kh.y;
+        aab += at.z * bh.z; aak += at.z * kh.z; brb += rt.z * bh.z; brk += rt.z * kh.z;
+        aab += at.w * bh.w; aak += at.w * kh.w; brb += rt.w * bh.w; brk += rt.w * kh.w;
       }
     }
     Aab[t][j] = (j < t) ? aab : 0.f;
@@ -205,13 +216,17 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
   }
   __syncthreads();
   float* out = rec + ((size_t)c * H + h) * REC;
-  // 5. What = T At (CL x KD), PU = T Aak (CL x CL)
-  for (int i = tid; i < CL * KD; i += 256) {
-    const int t = i / KD, k = i % KD;
-    float v = 0.f;
-    for (int q = 0; q <= t; ++q) v += Tm[t][q] * sa_[q * RS + k];
-    Wh[t * RS + k] = v;
-    out[OFF_W + t * KD + k] = v;
+  // 5. What = T At (CL x KD; 4 consecutive columns per thread), PU = T Aak (CL x CL)
+  {
+    const int t = tid >> 4, k0 = (tid & 15) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q <= t; ++q) {
+      const float tm = Tm[t][q];
+      const float4 a = *reinterpret_cast<const float4*>(sa_ + q * RSA + k0);
+      v.x += tm * a.x; v.y += tm * a.y; v.z += tm * a.z; v.w += tm * a.w;
+    }
+    *reinterpret_cast<float4*>(Wh + t * RSA + k0) = v;
+    *reinterpret_cast<float4*>(out + OFF_W + t * KD + k0) = v;
   }
   {
     const int t = tid >> 4, j = tid & 15;
@@ -220,15 +235,21 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
     PU[t][j] = v;
   }
   __syncthreads();
-  // 6. Q = Rt + Brb What, PY = Brb PU + Brk, Bt/Kt/gL
-  for (int i = tid; i < CL * KD; i += 256) {
-    const int t = i / KD, k = i % KD;
-    float v = sr_[t * RS + k];
-    for (int q = 0; q <= t; ++q) v += Brb[t][q] * Wh[q * RS + k];
-    out[OFF_Q + t * KD + k] = v;
-    const float gl = glv[k];
-    out[OFF_B + t * KD + k] = sb_[t * RS + k] * gl;
-    if (t == 0) out[OFF_G + k] = gl;
+  // 6. Q = Rt + Brb What, PY = Brb PU + Brk, Bt/Kt/gL (4 consecutive columns per thread)
+  {
+    const int t = tid >> 4, k0 = (tid & 15) * 4;
+    float4 v = *reinterpret_cast<const float4*>(sr_ + t * RSA + k0);
+    for (int q = 0; q <= t; ++q) {
+      const float b = Brb[t][q];
+      const float4 w4 = *reinterpret_cast<const float4*>(Wh + q * RSA + k0);
+      v.x += b * w4.x; v.y += b * w4.y; v.z += b * w4.z; v.w += b * w4.w;
+    }
+    *reinterpret_cast<float4*>(out + OFF_Q + t * KD + k0) = v;
+    const float4 gl = *reinterpret_cast<const float4*>(glv + k0);
+    const float4 bt = *reinterpret_cast<const float4*>(sb_ + t * RSB + k0);
+    *reinterpret_cast<float4*>(out + OFF_B + t * KD + k0) =
+        make_float4(bt.x * gl.x, bt.y * gl.y, bt.z * gl.z, bt.w * gl.w);
+    if (t == 0) *reinterpret_cast<float4*>(out + OFF_G + k0) = gl;
   }
   {
     const int t = tid >> 4, j = tid & 15;
@@ -245,11 +266,12 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
 #pragma unroll 4
     for (int j = 0; j < CL; ++j) {
       const float a = PU[t][j], b = PY[t][j];
+      const float4 v4 = *reinterpret_cast<const float4*>(sv_ + j * RSA + r0);
+      const float vj[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const float vj = sv_[j * RS + r0 + r];
-        pu[r] += a * vj;
-        py[r] += b * vj;
+        pu[r] += a * vj[r];
+        py[r] += b * vj[r];
       }
     }
 #pragma unroll
@@ -264,12 +286,9 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
     float u[4][4] = {};
 #pragma unroll 2
     for (int j = 0; j < CL; ++j) {
-      float vv[4], kk[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        vv[e] = sv_[j * RS + r0 + e];
-        kk[e] = sk_[j * RS + k0 + e];
-      }
+      const float4 v4 = *reinterpret_cast<const float4*>(sv_ + j * RSA + r0);
+      const float4 k4 = *reinterpret_cast<const float4*>(sk_ + j * RSB + k0);
+      const float vv[4] = {v4.x, v4.y, v4.z, v4.w}, kk[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
