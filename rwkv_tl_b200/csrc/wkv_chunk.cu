@@ -160,20 +160,34 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
     sb_[qb] = b.x; sb_[qb + 1] = b.y;
   }
   __syncthreads();
-  // 2. cumulative log decay per column, then decay-scaled vectors
+  // 2. cumulative log decay per column (summed in t order by one thread per column), then
+  // the decay-scaled vectors by all threads (column k, rows 4 tq .. 4 tq + 3)
   if (tid < KD) {
-    float g = 0.f, egp = 1.f;  // e^{G_{t-1}}, carried
+    float lw[CL];
+#pragma unroll
+    for (int t = 0; t < CL; ++t) lw[t] = sg[t * RSA + tid];
+    float g = 0.f;
+#pragma unroll
     for (int t = 0; t < CL; ++t) {
-      g += sg[t * RSA + tid];
-      const float eg = expf(g), egi = 1.0f / eg;
-      sa_[t * RSA + tid] *= egp;
-      sb_[t * RSB + tid] *= egi;
-      sk_[t * RSB + tid] *= egi;
-      sr_[t * RSA + tid] *= eg;
+      g += lw[t];
       sg[t * RSA + tid] = g;
+    }
+  }
+  __syncthreads();
+  {
+    const int k = tid & (KD - 1), tq = tid / KD;
+    float egp = tq ? expf(sg[(4 * tq - 1) * RSA + k]) : 1.f;  // e^{G_{t-1}}
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = 4 * tq + i;
+      const float eg = expf(sg[t * RSA + k]), egi = 1.0f / eg;
+      sa_[t * RSA + k] *= egp;
+      sb_[t * RSB + k] *= egi;
+      sk_[t * RSB + k] *= egi;
+      sr_[t * RSA + k] *= eg;
       egp = eg;
     }
-    glv[tid] = expf(g);
+    if (tq == CL / 4 - 1) glv[k] = egp;  // e^{G_L}
   }
   __syncthreads();
   // 3. the four L x L interaction matrices
@@ -216,17 +230,20 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
   }
   __syncthreads();
   float* out = rec + ((size_t)c * H + h) * REC;
-  // 5. What = T At (CL x KD; 4 consecutive columns per thread), PU = T Aak (CL x CL)
-  {
-    const int t = tid >> 4, k0 = (tid & 15) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  // 5. What = T At (CL x KD), PU = T Aak (CL x CL). Triangular rows are paired: warp w
+  // computes rows w and CL - 1 - w (two columns per lane), 17 row steps for every warp.
+  const int wp = tid >> 5, k2 = (tid & 31) * 2;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int t = half ? CL - 1 - wp : wp;
+    float2 v = make_float2(0.f, 0.f);
     for (int q = 0; q <= t; ++q) {
       const float tm = Tm[t][q];
-      const float4 a = *reinterpret_cast<const float4*>(sa_ + q * RSA + k0);
-      v.x += tm * a.x; v.y += tm * a.y; v.z += tm * a.z; v.w += tm * a.w;
+      const float2 a = *reinterpret_cast<const float2*>(sa_ + q * RSA + k2);
+      v.x += tm * a.x; v.y += tm * a.y;
     }
-    *reinterpret_cast<float4*>(Wh + t * RSA + k0) = v;
-    *reinterpret_cast<float4*>(out + OFF_W + t * KD + k0) = v;
+    *reinterpret_cast<float2*>(Wh + t * RSA + k2) = v;
+    *reinterpret_cast<float2*>(out + OFF_W + t * KD + k2) = v;
   }
   {
     const int t = tid >> 4, j = tid & 15;
@@ -235,21 +252,21 @@ __global__ void __launch_bounds__(256, PREP_MINB) k_chunk_prep(
     PU[t][j] = v;
   }
   __syncthreads();
-  // 6. Q = Rt + Brb What, PY = Brb PU + Brk, Bt/Kt/gL (4 consecutive columns per thread)
-  {
-    const int t = tid >> 4, k0 = (tid & 15) * 4;
-    float4 v = *reinterpret_cast<const float4*>(sr_ + t * RSA + k0);
+  // 6. Q = Rt + Brb What, PY = Brb PU + Brk, Bt/Kt/gL (rows paired as in step 5)
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int t = half ? CL - 1 - wp : wp;
+    float2 v = *reinterpret_cast<const float2*>(sr_ + t * RSA + k2);
     for (int q = 0; q <= t; ++q) {
       const float b = Brb[t][q];
-      const float4 w4 = *reinterpret_cast<const float4*>(Wh + q * RSA + k0);
-      v.x += b * w4.x; v.y += b * w4.y; v.z += b * w4.z; v.w += b * w4.w;
+      const float2 w2 = *reinterpret_cast<const float2*>(Wh + q * RSA + k2);
+      v.x += b * w2.x; v.y += b * w2.y;
     }
-    *reinterpret_cast<float4*>(out + OFF_Q + t * KD + k0) = v;
-    const float4 gl = *reinterpret_cast<const float4*>(glv + k0);
-    const float4 bt = *reinterpret_cast<const float4*>(sb_ + t * RSB + k0);
-    *reinterpret_cast<float4*>(out + OFF_B + t * KD + k0) =
-        make_float4(bt.x * gl.x, bt.y * gl.y, bt.z * gl.z, bt.w * gl.w);
-    if (t == 0) *reinterpret_cast<float4*>(out + OFF_G + k0) = gl;
+    *reinterpret_cast<float2*>(out + OFF_Q + t * KD + k2) = v;
+    const float2 gl = *reinterpret_cast<const float2*>(glv + k2);
+    const float2 bt = *reinterpret_cast<const float2*>(sb_ + t * RSB + k2);
+    *reinterpret_cast<float2*>(out + OFF_B + t * KD + k2) = make_float2(bt.x * gl.x, bt.y * gl.y);
+    if (t == 0) *reinterpret_cast<float2*>(out + OFF_G + k2) = gl;
   }
   {
     const int t = tid >> 4, j = tid & 15;
