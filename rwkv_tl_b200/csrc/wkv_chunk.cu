@@ -802,7 +802,8 @@ __global__ void __launch_bounds__(256) k_seg_combine(const int* __restrict__ seg
 // grid = (max segments, H), block = 256 (8 warps). Segments g >= 1 of multi-segment
 // sequences: for each chunk, y = yf32 + (Q Phi) S_g^T on the tensor cores (3xTF32),
 // rounded to fp16 once (like the reference's y store). Warp w owns state rows 8w..8w+7;
-// S_g is loaded once per segment, the next chunk's Q Phi is prefetched into registers.
+// S_g is loaded once per segment, the next chunk's Q Phi and fp32 partial outputs are
+// prefetched into registers.
 __global__ void __launch_bounds__(256) k_seg_fix(const int* __restrict__ cu,
                                                  const int* __restrict__ chunk_cu,
                                                  const int* __restrict__ seg_cu, int S,
@@ -826,22 +827,31 @@ __global__ void __launch_bounds__(256) k_seg_fix(const int* __restrict__ cu,
   }
   const int lane = tid & 31, warp = tid >> 5, gq = lane >> 2, q = lane & 3;
   const int m_end = cu[s + 1];
-  float4 nq = reinterpret_cast<const float4*>(qt + ((size_t)c0 * H + h) * (CL * KD))[tid];
-  for (int c = c0; c < c1; ++c) {
-    *reinterpret_cast<float4*>(Qs + (tid >> 4) * WQ_LD + (tid & 15) * 4) = nq;
-    __syncthreads();
-    if (c + 1 < c1) nq = reinterpret_cast<const float4*>(qt + ((size_t)(c + 1) * H + h) * (CL * KD))[tid];
-    const int nb0 = warp * 8;
+  const int nb0 = warp * 8, v = nb0 + 2 * q;
+  // a chunk's fp32 partial outputs (rows gq and gq + 8 of the chunk, columns v, v + 1)
+  auto load_y = [&](int c, float2 (&yv)[2]) {
     const int m0 = cu[s] + (c - chunk_cu[s]) * CL;
-    const int v = nb0 + 2 * q;
-    // this chunk's fp32 partial outputs, fetched before the products (latency overlap)
-    float2 yv[2];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int m = m0 + gq + 8 * half;
       yv[half] = m < m_end ? *reinterpret_cast<const float2*>(yf32 + (size_t)m * C + h * KD + v)
                            : make_float2(0.f, 0.f);
     }
+  };
+  // Q Phi and the partial outputs of the next chunk are fetched one chunk ahead
+  float4 nq = reinterpret_cast<const float4*>(qt + ((size_t)c0 * H + h) * (CL * KD))[tid];
+  float2 yv[2], ny[2];
+  load_y(c0, ny);
+  for (int c = c0; c < c1; ++c) {
+    *reinterpret_cast<float4*>(Qs + (tid >> 4) * WQ_LD + (tid & 15) * 4) = nq;
+    yv[0] = ny[0];
+    yv[1] = ny[1];
+    __syncthreads();
+    if (c + 1 < c1) {
+      nq = reinterpret_cast<const float4*>(qt + ((size_t)(c + 1) * H + h) * (CL * KD))[tid];
+      load_y(c + 1, ny);
+    }
+    const int m0 = cu[s] + (c - chunk_cu[s]) * CL;
     float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int kb = 0; kb < KD; kb += 8) {
