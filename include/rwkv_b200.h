@@ -183,8 +183,9 @@ int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const void* k, con
  * rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H) is at most 32 MiB and
  * returns RWKV_ERR_SPACE otherwise. The first call on a device looks up the
  * array's address (do it before any stream capture). All calls share the one
- * array: calls that overlap on the GPU (different streams) race. No
- * counterpart in the reference. */
+ * array: calls that overlap on the GPU (different streams) race. The looked-up
+ * address is cached per device; after cudaDeviceReset in the same process it is
+ * stale, so do not call this again after a reset. No counterpart in the reference. */
 int rwkv7_dplr_chunked_noalloc(void* S, const void* r, const void* w, const void* k,
                                const void* v, const void* a, const void* b, void* y, int n_seq,
                                int T, int H, void* stream);

@@ -17,6 +17,7 @@
 // (chunk, head); k_chunk_scan then walks the chunks of each sequence in order
 // with the fp32 state of 8 rows in registers (one warp per row). All math is
 // fp32; exponents stay within one chunk (|G| <= 16 * 0.6066), so no overflow.
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -1086,6 +1087,8 @@ int wkv_chunk_bad_flag() {
 
 extern "C" size_t rwkv7_dplr_chunked_workspace_bytes(int n_seq, int T, int H) {
   if (n_seq <= 0 || T <= 0 || H <= 0) return 0;
+  // token counts are int inside the kernels: refuse what does not fit
+  if ((size_t)n_seq * (size_t)T > (size_t)INT_MAX) return 0;
   const size_t cu = ((size_t)(n_seq + 1) * 2 * sizeof(int) + 255) & ~size_t(255);
   return cu + wkv_chunk_record_bytes(n_seq * T, n_seq, H);
 }
@@ -1100,6 +1103,10 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
                    T, H);
     return RWKV_ERR_ARG;
   }
+  if ((size_t)n_seq * T * H * KD > ((size_t)1 << 31)) {
+    rwkv_set_error("rwkv7_dplr_chunked: problem too large (%d x %d x %d)", n_seq, T, H);
+    return RWKV_ERR_ARG;
+  }
   if (reinterpret_cast<uintptr_t>(S) & 15) {
     rwkv_set_error("rwkv7_dplr_chunked: S must be 16-byte aligned");
     return RWKV_ERR_ARG;
@@ -1109,10 +1116,6 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
     rwkv_set_error("rwkv7_dplr_chunked: workspace needs %zu bytes, 256-aligned (got %zu)", need,
                    workspace_bytes);
     return RWKV_ERR_SPACE;
-  }
-  if ((size_t)n_seq * T * H * KD > ((size_t)1 << 31)) {
-    rwkv_set_error("rwkv7_dplr_chunked: problem too large (%d x %d x %d)", n_seq, T, H);
-    return RWKV_ERR_ARG;
   }
   cudaStream_t st = (cudaStream_t)stream;
   int* cu = static_cast<int*>(workspace);
@@ -1140,7 +1143,10 @@ extern "C" int rwkv7_dplr_chunked(void* S, const void* r, const void* w, const v
 // these 32 MiB until the process exits. In host code `g_noalloc_scratch` is
 // only a host-side stand-in for the symbol, never a device address; the device
 // address comes from cudaGetSymbolAddress, once per device, on that device's
-// first call (make that first call before any stream capture).
+// first call (make that first call before any stream capture). That cached
+// address belongs to the device's current context: after cudaDeviceReset in
+// the host process it is stale, so do not call this entry point again after a
+// device reset in the same process.
 namespace {
 constexpr size_t NOALLOC_BYTES = (size_t)32 << 20;
 }
@@ -1155,6 +1161,10 @@ extern "C" int rwkv7_dplr_chunked_noalloc(void* S, const void* r, const void* w,
   rwkv_chain_begin();
   if (n_seq <= 0 || T <= 0 || H <= 0) {
     rwkv_set_error("rwkv7_dplr_chunked_noalloc: bad size (n_seq=%d, T=%d, H=%d)", n_seq, T, H);
+    return RWKV_ERR_ARG;
+  }
+  if ((size_t)n_seq * T * H * KD > ((size_t)1 << 31)) {
+    rwkv_set_error("rwkv7_dplr_chunked_noalloc: problem too large (%d x %d x %d)", n_seq, T, H);
     return RWKV_ERR_ARG;
   }
   const size_t need = rwkv7_dplr_chunked_workspace_bytes(n_seq, T, H);

@@ -48,6 +48,7 @@ class CUDAGraph(RWKV7Model):
         self._max = max_graphs
         self._graphs: OrderedDict = OrderedDict()
         self._failed: set = set()
+        self._keep: dict = {}
 
     def __getattr__(self, name):
         model = self.__dict__.get("model")
@@ -63,6 +64,7 @@ class CUDAGraph(RWKV7Model):
         return e
 
     def _put(self, key, e):
+        e.extra = self._keep.pop(key, None)
         self._graphs[key] = e
         while len(self._graphs) > self._max:
             self._graphs.popitem(last=False)
@@ -80,6 +82,11 @@ class CUDAGraph(RWKV7Model):
             with torch.cuda.graph(g, stream=s):
                 run_on(live_state)
             torch.cuda.current_stream(self.w.device).wait_stream(s)
+            # The graph holds the addresses of the model's scratch buffers as they
+            # were during capture. The model replaces a buffer when a later call needs
+            # more bytes; keeping the captured ones referenced here means they are
+            # never returned to the allocator while this graph can still replay.
+            self._keep[key] = (self.model._ws, self.model._ws_dec)
             return g
         except Exception as e:  # noqa: BLE001 - capture problem -> eager
             warnings.warn(f"CUDA-Graph {name} capture failed ({e}); running eager.", stacklevel=3)
@@ -100,6 +107,7 @@ class CUDAGraph(RWKV7Model):
                 out["logits"], _ = self.model.decode(tok, st)
 
             scratch = State(self.L, self.C, 64, device=self.w.device)
+            self.model._const((S._slot,))  # built outside the capture
             g = self._capture(key, run, scratch, S, "decode")
             if g is not None:
                 e = _Entry(g, tok, out["logits"])
@@ -124,6 +132,8 @@ class CUDAGraph(RWKV7Model):
         if e is None and key not in self._failed:
             buf = torch.zeros(T, dtype=torch.long, device=self.w.device)
             scratch = State(self.L, self.C, 64, device=self.w.device)
+            self.model._const((S._slot,))
+            self.model._const((0, T))
             g = self._capture(key, lambda st: self.model.prefill(buf, st), scratch, S,
                               f"prefill(T={T})")
             if g is not None:

@@ -71,7 +71,8 @@ def run_cases(model, w, dtype, tokens) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("RWKV_TL_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("RWKV_TL_REFERENCE"), required="RWKV_TL_REFERENCE" not in os.environ,
+                    help="path of a yuyi2439/rwkv-tl checkout (or set RWKV_TL_REFERENCE)")
     args = ap.parse_args()
     sys.path[:0] = [os.path.join(args.reference, "src"), args.reference]
     torch.set_num_threads(os.cpu_count() or 1)

@@ -168,6 +168,48 @@ def test_graph_wrapper_matches_eager():
         assert torch.equal(x["rnn"], y["rnn"])
 
 
+def test_graph_replay_after_workspace_growth():
+    """A captured graph keeps working after later calls grew the model's scratch.
+
+    Capture a short prefill, then a longer one and an eager prefill longer than any
+    graph, then replay the first graph: it must still match eager. Same for a graphed
+    B=1 decode (persistent kernel, C=768) replayed after a B=4 decode_batch and a
+    B=64 token-batch decode have grown both scratch buffers.
+    """
+    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 5)
+    gm = make_rwkv7(torch.device("cuda"), backend="b200")(m.w)
+    toks = _tokens(400, 4096, 17)
+    Sg, Se = State(m.L, m.C, 64, device="cuda"), State(m.L, m.C, 64, device="cuda")
+    gm.prefill(torch.tensor(toks[:9], device="cuda"), Sg)        # capture T=9
+    m.prefill(torch.tensor(toks[:9], device="cuda"), Se)
+    big = State(m.L, m.C, 64, device="cuda")
+    gm.prefill(torch.tensor(toks[:60], device="cuda"), big)      # capture T=60 (more scratch)
+    gm.prefill(torch.tensor(toks[:400], device="cuda"), big)     # eager, larger still
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    junk = torch.full((64 << 20,), 7, dtype=torch.uint8, device="cuda")  # reuse freed blocks
+    gm.prefill(torch.tensor(toks[9:18], device="cuda"), Sg)      # replay T=9
+    m.prefill(torch.tensor(toks[9:18], device="cuda"), Se)
+    del junk
+    for x, y in zip(Sg.tmix, Se.tmix):
+        assert torch.equal(x["rnn"], y["rnn"])
+    a, _ = gm.decode(torch.tensor(5, device="cuda"), Sg)        # capture decode B=1
+    b, _ = m.decode(torch.tensor(5, device="cuda"), Se)
+    bs = BatchedState(m.L, m.C, 64, device="cuda")
+    gm.decode_batch(torch.arange(4, device="cuda"), bs)          # B=4: larger GEMV scratch
+    gm.decode_batch(torch.arange(64, device="cuda"), bs)         # token batch scratch
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    junk = torch.full((64 << 20,), 7, dtype=torch.uint8, device="cuda")
+    a, _ = gm.decode(torch.tensor(11, device="cuda"), Sg)       # replay
+    b, _ = m.decode(torch.tensor(11, device="cuda"), Se)
+    del junk
+    # the persistent kernel sums with float atomics: equal to within last-bit noise
+    assert (a.float() - b.float()).abs().max() < 2e-2
+    for x, y in zip(Sg.tmix, Se.tmix):
+        assert (x["rnn"] - y["rnn"]).norm() <= 1e-4 * y["rnn"].norm()
+
+
 def test_foreign_state_layout_roundtrip():
     """A State whose dict entries were rebound still works (staged copy in/out)."""
     m, o = _pair(CONFIG_TINY, 1)
