@@ -140,6 +140,15 @@ unsigned long long rwkv_b200_launch_count(void);
  * bounded wait for a chunk record (bit 2). Reading clears it.
  * Synchronous (reads device memory). */
 int rwkv_b200_device_error(void);
+/* Makes one of the library's bounded device waits run out on purpose, to show that
+ * failure detection fires and the context stays usable: which = 0 the GEMM pipeline's
+ * mbarrier wait (sets bit 0 of rwkv_b200_device_error, ~1 s), 1 the persistent decode
+ * kernel's grid-barrier and mbarrier waits (bit 1, ~0.4 s), 2 the chunk scan's record
+ * wait (bit 2, ~0.2 s). Each launches one small kernel that runs the same wait
+ * function on a barrier nothing signals; it writes an int at scratch + 16 (nonzero:
+ * the wait gave up). scratch: 32 zeroed, 16-byte aligned device bytes. No GPU fault,
+ * trap or hang is involved. No counterpart in the reference (it has no device waits). */
+int rwkv_b200_wait_selftest(int which, void* scratch, void* stream);
 
 /* wkv7 DPLR step, batched over n_seq independent sequences (T = 1):
  *   sa[v] = sum_j S[v,j] a[j];  S[v,k] = S[v,k] w[k] + sa[v] b[k] + v[v] k[k];

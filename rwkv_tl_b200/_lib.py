@@ -19,6 +19,7 @@ EXPORTED = (
     "rwkv_b200_abi_version",
     "rwkv_b200_launch_count",
     "rwkv_b200_device_error",
+    "rwkv_b200_wait_selftest",
     "rwkv7_dplr_step",
     "rwkv7_dplr_seq",
     "rwkv7_wkv_gn_step",
@@ -103,6 +104,8 @@ def load() -> C.CDLL:
     lib.rwkv_b200_abi_version.restype = C.c_int
     lib.rwkv_b200_launch_count.restype = C.c_ulonglong
     lib.rwkv_b200_device_error.restype = C.c_int
+    lib.rwkv_b200_wait_selftest.restype = C.c_int
+    lib.rwkv_b200_wait_selftest.argtypes = [C.c_int, vp, vp]
     for name in ("rwkv7_dplr_step", "rwkv7_dplr_seq"):
         f = getattr(lib, name)
         f.restype = C.c_int

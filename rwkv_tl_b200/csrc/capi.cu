@@ -62,6 +62,27 @@ extern "C" int rwkv_b200_device_error(void) {
   return a | (b << 1) | (c << 2);
 }
 
+int wait_selftest_tc(int* out, cudaStream_t st);
+int wait_selftest_persist(void* bar, int* out, cudaStream_t st);
+int wait_selftest_scan(int* out, cudaStream_t st);
+extern "C" int rwkv_b200_wait_selftest(int which, void* scratch, void* stream) {
+  rwkv_chain_begin();
+  if (!scratch || (reinterpret_cast<uintptr_t>(scratch) & 15)) {
+    rwkv_set_error("rwkv_b200_wait_selftest: scratch must be 32 zeroed, 16-byte aligned bytes");
+    return RWKV_ERR_ARG;
+  }
+  int* out = reinterpret_cast<int*>(static_cast<char*>(scratch) + 16);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (which) {
+    case 0: return wait_selftest_tc(out, st);
+    case 1: return wait_selftest_persist(scratch, out, st);
+    case 2: return wait_selftest_scan(out, st);
+    default:
+      rwkv_set_error("rwkv_b200_wait_selftest: which must be 0, 1 or 2 (got %d)", which);
+      return RWKV_ERR_ARG;
+  }
+}
+
 extern "C" unsigned long long rwkv_b200_launch_count(void) {
   return __atomic_load_n(&g_launches, __ATOMIC_RELAXED);
 }

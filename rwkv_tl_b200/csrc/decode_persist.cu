@@ -1312,6 +1312,29 @@ extern "C" int rwkv7_decode_persist_stamps(unsigned long long* out) {
 }
 #endif
 
+// Self-test of the persistent kernel's bounded waits, with the same device functions:
+// a grid barrier whose target the single CTA can never reach, then an mbarrier that
+// nothing arrives on. Both must give up after WAIT_NS, set the device error flag and
+// return. `bar` is 16 zeroed bytes of device memory supplied by the caller.
+namespace {
+__global__ void k_wait_selftest_persist(GridBar* bar, int* out) {
+  __shared__ int s_ok;
+  __shared__ __align__(8) uint64_t mb;
+  const bool grid_ok = grid_sync(bar, 2u, &s_ok, [] {});
+  if (threadIdx.x == 0) {
+    mbar_init(&mb, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    bar->abort = 0;  // the grid wait raised it; clear so the mbarrier wait runs to its limit
+    const bool mb_ok = mbar_wait(&mb, 0, bar);
+    out[0] = (grid_ok ? 0 : 1) | (mb_ok ? 0 : 2);
+  }
+}
+}  // namespace
+int wait_selftest_persist(void* bar, int* out, cudaStream_t st) {
+  return rwkv_launch("wait_selftest_persist", k_wait_selftest_persist, dim3(1), dim3(64), 0, st,
+                     static_cast<GridBar*>(bar), out);
+}
+
 int decode_persist_timeout_flag() {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_persist_timeout, sizeof(int));

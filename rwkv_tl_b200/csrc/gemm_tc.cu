@@ -31,7 +31,7 @@ namespace {
 
 constexpr int BM = 128, BK = 64;
 constexpr int NTHREADS = 192;
-constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr uint64_t WAIT_NS = 1000000000ull;  // 1 s: a pipeline barrier gave up
 
 __device__ int g_tc_timeout = 0;
 
@@ -80,10 +80,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait; false (and the global error flag set) if the phase never completes.
+__device__ __forceinline__ uint64_t tc_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait; false (and the global error flag set) if the phase has not completed
+// within WAIT_NS of wall time (the timer is read once per 256 polls).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = tc_globaltimer();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && tc_globaltimer() - t0 > WAIT_NS) break;
+  }
   atomicExch(&g_tc_timeout, 1);
   return false;
 }
@@ -906,6 +917,23 @@ int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, 
              : epi == RWKV_EPI_LORA_ACT  ? k_splitk_reduce<RWKV_EPI_LORA_ACT>
                                          : k_splitk_reduce<RWKV_EPI_LORA_ACT2>;
   return rwkv_launch("splitk_reduce", red, rgrid, dim3(256), 0, st, rp);
+}
+
+// Self-test of the pipeline's bounded wait: one thread waits on an mbarrier that
+// nothing ever arrives on, through the same mbar_wait the GEMM kernels use. The wait
+// must give up, set the device error flag and let the kernel return.
+namespace {
+__global__ void k_wait_selftest_tc(int* out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    out[0] = mbar_wait(&bar, 0) ? 0 : 1;
+  }
+}
+}  // namespace
+int wait_selftest_tc(int* out, cudaStream_t st) {
+  return rwkv_launch("wait_selftest_tc", k_wait_selftest_tc, dim3(1), dim3(32), 0, st, out);
 }
 
 // Host read of the device timeout flag (cleared on read); nonzero means a bounded wait gave up.

@@ -1075,6 +1075,23 @@ __global__ void k_uniform_cu(int* cu, int S, int T) {
   if (i <= S) cu[i] = i * T;
 }
 
+// Self-test of the chunk scan's bounded record wait (sc_mbar_wait) on an mbarrier
+// that nothing arrives on: it must give up after SCAN_WAIT_NS, set bit 2 of the
+// device error word and return.
+namespace {
+__global__ void k_wait_selftest_scan(int* out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    sc_mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    out[0] = sc_mbar_wait(&bar, 0) ? 0 : 1;
+  }
+}
+}  // namespace
+int wait_selftest_scan(int* out, cudaStream_t st) {
+  return rwkv_launch("wait_selftest_scan", k_wait_selftest_scan, dim3(1), dim3(32), 0, st, out);
+}
+
 int wkv_chunk_bad_flag() {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_chunk_bad, sizeof(int));
