@@ -147,10 +147,30 @@ def cpu_decode_rate(n_tokens: int, threads: int) -> dict:
         o.decode(1000 + i, S)
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
+    cfg0 = cpu_config0(threads)
     return {"value": 1.0 / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "config0": cfg0,
             "sample": f"0.4B fp32 decode (oracle port of demo/rwkv7_torch.py), 1 sequence, "
                       f"{n_tokens} tokens after 1 warm-up, median {med * 1e3:.1f} ms/token; "
                       "batched CPU decode loops over sequences, so tokens/s is per token"}
+
+
+def cpu_config0(threads: int) -> dict:
+    """BASELINE config 0 on the CPU port: 0.1B fp32, an 8-token prompt (forward), then
+    16 greedy tokens (``demo/rwkv7_torch.py:149-171``)."""
+    from oracle.rwkv7_oracle import OracleState, OracleWeights, RWKV7Oracle
+    from rwkv_tl_b200.synth import CONFIG_0_1B, synth_checkpoint
+
+    torch.set_num_threads(threads)
+    o = RWKV7Oracle(OracleWeights(synth_checkpoint(CONFIG_0_1B, seed=0), mode="fp32"))
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, 65536, (8,), generator=g).tolist()
+    S = OracleState(o.w.L, o.w.C)
+    t0 = time.perf_counter()
+    _, _ = o.generate_greedy(prompt, 16, S)
+    dt = time.perf_counter() - t0
+    return {"workload": "0.1B fp32, forward(8-token prompt) + 16 greedy tokens, 1 sequence",
+            "seconds": dt, "tokens_per_s": (8 + 15) / dt, "cores": threads}
 
 
 def run_reference(args, world, rank):
@@ -225,7 +245,9 @@ def run_b200(args, world, rank, local):
     model.model.decode_batch(tokens, state)
     launches_per_step = int(lib.rwkv_b200_launch_count() - c0)
 
-    step = lambda: model.decode_batch(tokens, state)  # noqa: E731 (graph replay)
+    logits_buf = torch.empty(B, cfg.vocab, dtype=torch.float16, device=dev)
+    # graph replay writing into the caller's buffer (no copy of the [B, V] logits)
+    step = lambda: model.decode_batch(tokens, state, logits=logits_buf)  # noqa: E731
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -243,7 +265,7 @@ def run_b200(args, world, rank, local):
 
     def e2e_step():
         dev_tok.copy_(host_tok, non_blocking=True)
-        logits = model.decode_batch(dev_tok, state)
+        logits = model.decode_batch(dev_tok, state, logits=logits_buf)
         host_out.copy_(logits.argmax(-1), non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
 
@@ -378,8 +400,103 @@ def side_measurements(model, w, dev, stream, step_bytes_of, hbm_gbs) -> dict:
     f()
     ms = timed(f, 3, stream)
     out["prefill_T4096"] = {"tokens_per_s": 4096 / (ms * 1e-3), "ms": ms}
+    # prefill against the tensor roofline: the projections' GEMM flops (2 x parameters
+    # of r/k/v, LoRA down + up, W_o, FFN key + value, per token; prefill runs no head)
+    # plus the wkv recurrence's (~5 x 64 x 64 multiply-adds per head per token)
+    C, L = w.C, w.L
+    gemm_flop = 2 * L * (12 * C * C + 2 * 288 * C) * 4096
+    wkv_flop = 2 * L * (C // 64) * 5 * 64 * 64 * 4096
+    pk, pk_kind = peaks()
+    tf = (gemm_flop + wkv_flop) / (ms * 1e-3) / 1e12
+    out["prefill_roofline"] = {"bound": "tensor", "flop_per_call": gemm_flop + wkv_flop,
+                               "achieved": tf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                               "frac": tf / pk["bf16_tflops"], "peak_kind": pk_kind,
+                               "T": 4096, "ms": ms}
+    out.update(config_sweeps(model, w, dev, stream, pk["hbm_gbs"]))
     out["continuous_batching"] = continuous_batching(model, w, dev, stream, n_seqs=256,
                                                      max_new=128, max_batch=256)
+    return out
+
+
+def config_sweeps(model, w, dev, stream, hbm_gbs) -> dict:
+    """The other BASELINE configs, timed beside the headline (rank 0, N=1):
+
+    * config 1: the isolated wkv7 kernels, H=16, B in {1, 8, 64}, T in {1, 64, 1024,
+      4096} (T=1: the one-token step kernel; T>1: the chunk-parallel kernel), against
+      HBM (fp16 r/w/k/v/a/b in + y out, fp32 state read + write);
+    * config 2: 0.1B decode at B in {1, 8, 64, 256} from random states (CUDA graph);
+    * config 3: 0.4B forward at T in {8, 64, 128, 1024, 4096} then 32 greedy decode
+      steps, one sequence.
+    """
+    from rwkv_tl_b200 import BatchedState, RWKV7Weight, State, _lib, make_rwkv7
+    from rwkv_tl_b200.synth import CONFIG_0_1B, synth_checkpoint
+
+    lib = _lib.load()
+    out: dict = {"config1_wkv_sweep": {}, "config2_0p1b_decode": {}, "config3_0p4b_prefill": {}}
+    H, h = 16, stream.cuda_stream
+    g = torch.Generator(device=dev).manual_seed(11)
+    for B in (1, 8, 64):
+        for T in (1, 64, 1024, 4096):
+            vec = [torch.randn(B, T, H, 64, generator=g, device=dev).half() for _ in range(7)]
+            S = 0.1 * torch.randn(B, H, 64, 64, generator=g, device=dev)
+            if T == 1:
+                f = lambda: _lib.check(lib.rwkv7_dplr_step(  # noqa: E731
+                    S.data_ptr(), *[t.data_ptr() for t in vec], B, H, h))
+            else:
+                nb = lib.rwkv7_dplr_chunked_workspace_bytes(B, T, H)
+                ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+                f = lambda: _lib.check(lib.rwkv7_dplr_chunked(  # noqa: E731
+                    S.data_ptr(), *[t.data_ptr() for t in vec], B, T, H, ws.data_ptr(), nb, h))
+            for _ in range(3):
+                f()
+            ms = timed(f, 20 if B * T <= 65536 else 5, stream)
+            algo = B * T * H * 64 * 2 * 7 + B * H * 64 * 64 * 4 * 2
+            out["config1_wkv_sweep"][f"B{B}_T{T}"] = {
+                "us": ms * 1e3, "tokens_per_s": B * T / (ms * 1e-3),
+                "hbm_frac": algo / (ms * 1e-3) / 1e9 / hbm_gbs}
+            del vec, S
+    # config 2: 0.1B
+    w1 = RWKV7Weight(synth_checkpoint(CONFIG_0_1B, seed=0, device=dev), device=dev)
+    m1 = make_rwkv7(dev, backend="b200")(w1)
+    gg = torch.Generator(device=dev).manual_seed(2)
+    for B in (1, 8, 64, 256):
+        st = BatchedState(w1.L, w1.C, B, device=dev)
+        st.rnn.normal_(0.0, 0.1, generator=gg)
+        tok = torch.randint(0, w1.V, (B,), generator=gg, device=dev)
+        lg = torch.empty(B, w1.V, dtype=torch.float16, device=dev)
+        f = lambda: m1.decode_batch(tok, st, logits=lg)  # noqa: E731
+        for _ in range(3):
+            f()
+        ms = timed(f, 50, stream)
+        out["config2_0p1b_decode"][f"B{B}"] = {"ms": ms, "tokens_per_s": B / (ms * 1e-3)}
+    del m1, w1
+    torch.cuda.empty_cache()
+    # config 3: 0.4B forward(T) + 32 greedy steps
+    for T in (8, 64, 128, 1024, 4096):
+        toks = torch.randint(0, w.V, (T,), generator=gg, device=dev)
+        S = State(w.L, w.C, 64, device=dev)
+
+        def run():
+            S.reset()
+            logits, _ = model.forward(toks, S)
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            for _ in range(32):
+                logits, _ = model.decode(logits.argmax(), S)
+            return e
+
+        run()
+        s0 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s0.record(stream)
+        mid = run()
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        fwd_ms, dec_ms = s0.elapsed_time(mid), mid.elapsed_time(e1)
+        out["config3_0p4b_prefill"][f"T{T}"] = {
+            "forward_ms": fwd_ms, "prefill_tokens_per_s": T / (fwd_ms * 1e-3),
+            "decode32_ms": dec_ms, "decode_tokens_per_s": 32 / (dec_ms * 1e-3)}
     return out
 
 
@@ -473,7 +590,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=256)
-    ap.add_argument("--cpu-tokens", type=int, default=4)
+    ap.add_argument("--cpu-tokens", type=int, default=16)
     ap.add_argument("--quick", action="store_true", help="skip side measurements / CPU baseline")
     ap.add_argument("--profile", choices=["decode", "prefill"], default=None,
                     help="profiling driver: run only K decode steps (--batch) or K prefills "

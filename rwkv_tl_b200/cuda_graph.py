@@ -11,7 +11,8 @@ and replays them. Differences, B200-side:
   addresses, a small LRU), so there is no copy of the whole state into and out
   of a shadow state around every replay (``demo/cuda_graph.py:124-126``);
   a ``State`` that is not bound to library-addressable blocks runs eagerly;
-* ``decode_batch`` is captured per (batch size, state, slots).
+* ``decode_batch`` is captured per (batch size, state, slots, output buffer); given
+  an output buffer it writes the logits there with no extra copy.
 
 Capture failures fall back to eager, with a warning, as in the reference.
 """
@@ -149,11 +150,16 @@ class CUDAGraph(RWKV7Model):
                      logits: Tensor | None = None) -> Tensor:
         tok = self.model._tokens(tokens)
         B = tok.numel()
-        key = ("decb", B, state.rnn.data_ptr(), None if slots is None else slots.data_ptr())
+        # A caller-provided `logits` buffer is captured as the graph's output (keyed by its
+        # address), so replays write straight into it; without one, the graph owns its
+        # buffer and the caller gets a copy, as with the reference's wrapper.
+        key = ("decb", B, state.rnn.data_ptr(), None if slots is None else slots.data_ptr(),
+               None if logits is None else logits.data_ptr())
         e = self._get(key)
         if e is None and key not in self._failed:
             buf = torch.zeros(B, dtype=torch.long, device=self.w.device)
-            lg = torch.empty(B, self.model.V, dtype=torch.float16, device=self.w.device)
+            lg = logits if logits is not None else torch.empty(
+                B, self.model.V, dtype=torch.float16, device=self.w.device)
             scratch = BatchedState(self.L, self.C, state.n_slots, device=self.w.device)
             g = self._capture(key, lambda st: self.model.decode_batch(buf, st, slots, lg), scratch,
                               state, f"decode_batch(B={B})")
@@ -165,7 +171,6 @@ class CUDAGraph(RWKV7Model):
         e.tok.copy_(tok, non_blocking=True)
         e.graph.replay()
         if logits is not None:
-            logits.copy_(e.logits)
             return logits
         return e.logits.clone()
 

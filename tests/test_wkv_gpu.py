@@ -89,7 +89,7 @@ def test_dplr_rejects_bad_args():
 def _batched_ref(S0, r, w, k, v, A, Bv):
     """Serial fp32 recurrence, batched over sequences: inputs [B, T, H, 64]."""
     S = S0.clone()
-    ys = torch.empty(r.shape, dtype=torch.float32)
+    ys = torch.empty(r.shape, dtype=torch.float32, device=S0.device)
     f = lambda t: t.float()  # noqa: E731
     r, w, k, v, A, Bv = map(f, (r, w, k, v, A, Bv))
     for t in range(r.shape[1]):
@@ -99,16 +99,19 @@ def _batched_ref(S0, r, w, k, v, A, Bv):
     return ys, S
 
 
-@pytest.mark.parametrize("B,T", [(1, 64), (8, 64), (1, 1024), (8, 1024), (64, 64), (1, 4096),
-                                 (3, 37)])
+@pytest.mark.parametrize("B,T", [(b, t) for b in (1, 8, 64) for t in (64, 1024, 4096)] + [(3, 37)])
 def test_dplr_chunked_config1(B, T):
-    """BASELINE config 1 sweep (H=16) through the chunk-parallel kernel."""
+    """BASELINE config 1 sweep (H=16, B in {1, 8, 64}, T in {64, 1024, 4096}) through the
+    chunk-parallel kernel; T=1 is the step kernel's test above. The serial fp32
+    reference runs in torch, on the GPU for the large cases."""
     from rwkv_tl_b200 import _lib
 
     lib = _lib.load()
     H = 16
     r, w, k, v, A, Bv, S0 = _inputs(B, T, H, seed=B * 10000 + T)
-    yref, Sref = _batched_ref(S0, r, w, k, v, A, Bv)
+    on = "cuda" if B * T > 8192 else "cpu"
+    yref, Sref = _batched_ref(*(t.to(on) for t in (S0, r, w, k, v, A, Bv)))
+    yref, Sref = yref.cpu(), Sref.cpu()
     dev = [t.contiguous().cuda() for t in (r, w, k, v, A, Bv)]
     S = S0.cuda().contiguous()
     y = torch.empty(B, T, H, 64, dtype=torch.float16, device="cuda")
