@@ -7,6 +7,20 @@
 
 namespace dec {
 
+// Order-independent accumulation across CTAs. Each partial sum is rounded once to a
+// 64-bit fixed-point integer with 32 fraction bits and added with an integer atomic.
+// Integer addition is associative, so the total -- and everything computed from it --
+// is the same bits whatever order the CTAs' additions land in (float atomics are not).
+// Range |partial| < 2^31 (activations are fp16, < 65504); resolution 2^-32, far below
+// the fp16 rounding that every sum receives.
+__device__ __forceinline__ void fx_add(long long* p, float v) {
+  atomicAdd(reinterpret_cast<unsigned long long*>(p),
+            static_cast<unsigned long long>(__float2ll_rn(v * 4294967296.0f)));
+}
+__device__ __forceinline__ float fx_val(long long x) {
+  return static_cast<float>(x) * 2.3283064365386963e-10f;  // 2^-32
+}
+
 constexpr int MAXB = 8;
 constexpr int NT = 256;
 

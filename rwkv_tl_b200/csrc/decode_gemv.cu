@@ -14,9 +14,9 @@
 //                LN1, six token-shift mixes, GEMV over [W_rkv (3C) ; W_lora_dn (288)] rows
 //   B (H CTAs)   LoRA-up + gates + L2 norm, wkv7 step on the head's fp32 state,
 //                GroupNorm + bonus + g gate, then the head's 64 columns of the output
-//                projection from shared memory: acc1 += W_o[:, head] @ yg (fp32 atomics)
+//                projection from shared memory: acc1 += W_o[:, head] @ yg (fixed-point atomics)
 //   C (4C/32)    x1 = x0 + fp16(acc1), LN2, mix, 32 FFN key rows -> relu^2 ->
-//                acc2 += W_fv[:, rows] @ h (fp32 atomics)
+//                acc2 += W_fv[:, rows] @ h (fixed-point atomics)
 //   head         x = x1 + fp16(acc2), ln_out, logits GEMV over V rows
 // The state x of each layer is written by the kernel after the one that read it
 // (every CTA of a kernel reads the old value). Workspace accumulators are zeroed
@@ -42,9 +42,9 @@ struct DecCommon {
   __half* rkv;     // [3, B, C]
   __half* ranks;   // [B, 288]
   __half* vfirst;  // [B, C]
-  float* acc1;     // [B, C] output-projection sums of this layer (zero on entry)
-  float* acc2;     // [B, C] FFN sums of this layer (zero on entry)
-  const float* acc2_prev;  // previous layer's FFN sums (layer > 0)
+  long long* acc1;     // [B, C] output-projection sums of this layer, fixed point (fx_add)
+  long long* acc2;     // [B, C] FFN sums of this layer (both zero on entry)
+  const long long* acc2_prev;  // previous layer's FFN sums (layer > 0)
   float* rnn;      // this layer's state: [slots, H, 64, 64]
   __half* tmix_x;  // [slots, C]
   __half* cmix_x;  // [slots, C]
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(NT) k_dec_a(const DecLayer L, const DecCommon 
 #pragma unroll
       for (int k = 0; k < CPL; ++k) {
         const size_t o = (size_t)bb * C + tid + NT * k;
-        x[b][k] = r16(h2f(P.x1[o]) + r16(P.acc2_prev[o]));
+        x[b][k] = r16(h2f(P.x1[o]) + r16(fx_val(P.acc2_prev[o])));
       }
     }
   }
@@ -275,7 +275,9 @@ __global__ void __launch_bounds__(NT) k_dec_b(const DecLayer L, const DecCommon 
 #pragma unroll
       for (int b = 0; b < NB; ++b) acc[b][g][jj & 1] += sr[b * RWKV_RANK_SUM + j] * wv;
     }
-    // a quarter covers at most two gates: add only the nonzero partials
+    // a quarter covers at most two gates: add only the nonzero partials (each gate's
+    // sum gets at most two additions onto zero, 0 + a + b == 0 + b + a in any order,
+    // so these shared-memory atomics are deterministic)
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int g0 = g == 0 ? 0 : (g == 1 ? 32 : (g == 2 ? 96 : 160));
@@ -402,8 +404,7 @@ __global__ void __launch_bounds__(NT) k_dec_b(const DecLayer L, const DecCommon 
       }
     }
     for (int b = 0; b < B; ++b)
-      atomicAdd(reinterpret_cast<float4*>(P.acc1 + (size_t)b * C + c0),
-                make_float4(acc[b][0], acc[b][1], acc[b][2], acc[b][3]));
+      for (int k = 0; k < 4; ++k) fx_add(P.acc1 + (size_t)b * C + c0 + k, acc[b][k]);
   }
   // new tmix state x (LN1 output) for this head's channels
   for (int i = tid; i < B * 64; i += NT) {
@@ -463,7 +464,7 @@ __global__ void __launch_bounds__(NT) k_dec_c(const DecLayer L, const DecCommon 
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
       const size_t o = (size_t)bb * C + tid + NT * k;
-      x[b][k] = r16(h2f(P.x0[o]) + r16(P.acc1[o]));
+      x[b][k] = r16(h2f(P.x0[o]) + r16(fx_val(P.acc1[o])));
       if (blockIdx.x == 0 && b < B) P.x1[o] = f2h(x[b][k]);
     }
   }
@@ -513,8 +514,7 @@ __global__ void __launch_bounds__(NT) k_dec_c(const DecLayer L, const DecCommon 
         }
       }
     for (int b = 0; b < B; ++b)
-      atomicAdd(reinterpret_cast<float4*>(P.acc2 + (size_t)b * C + 4 * tid),
-                make_float4(acc[b][0], acc[b][1], acc[b][2], acc[b][3]));
+      for (int k = 0; k < 4; ++k) fx_add(P.acc2 + (size_t)b * C + 4 * tid + k, acc[b][k]);
   }
 }
 
@@ -566,7 +566,7 @@ __global__ void __launch_bounds__(NT) k_dec_head(const __half* __restrict__ head
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
       const size_t o = (size_t)bb * C + tid + NT * k;
-      x[b][k] = r16(h2f(P.x1[o]) + r16(P.acc2[o]));
+      x[b][k] = r16(h2f(P.x1[o]) + r16(fx_val(P.acc2[o])));
     }
   }
   if (blockIdx.x == 0)
@@ -639,7 +639,7 @@ int launch_pdl(bool pdl, K kernel, dim3 grid, size_t smem, cudaStream_t st, cons
 
 struct DecWork {
   __half *x0, *x1, *xln1, *xln2, *rkv, *ranks, *vfirst;
-  float* acc;  // [L][2][B][C]
+  long long* acc;  // [L][2][B][C], fixed point
 };
 
 size_t carve_dec(void* base, DecWork* w, int L, int B, int C) {
@@ -658,7 +658,7 @@ size_t carve_dec(void* base, DecWork* w, int L, int B, int C) {
   d.rkv = (__half*)take(3 * BC * 2);
   d.ranks = (__half*)take((size_t)B * RWKV_RANK_SUM * 2);
   d.vfirst = (__half*)take(BC * 2);
-  d.acc = (float*)take((size_t)L * 2 * BC * 4);
+  d.acc = (long long*)take((size_t)L * 2 * BC * 8);
   if (w) *w = d;
   return off;
 }
@@ -668,7 +668,7 @@ int run_decode(const rwkv7_model* m, const int64_t* tokens, int B, const int* sl
                const rwkv7_state* state, void* logits, const DecWork& w, cudaStream_t st) {
   const int L = m->n_layer, C = m->n_embd, H = C / RWKV_HD;
   const size_t BC = (size_t)B * C;
-  if (cudaMemsetAsync(w.acc, 0, (size_t)L * 2 * BC * 4, st) != cudaSuccess)
+  if (cudaMemsetAsync(w.acc, 0, (size_t)L * 2 * BC * 8, st) != cudaSuccess)
     return rwkv_check_launch("decode_gemv memset");
   DecCommon P = {};
   P.B = B;

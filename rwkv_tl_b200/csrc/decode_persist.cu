@@ -3,6 +3,10 @@
 // every CTA is resident, with a grid barrier between the three phases of each layer
 // and before the head.
 //
+// Cross-CTA sums (the W_o and FFN-value partials) are fixed-point integer atomics
+// (fx_add), so a step's results do not depend on the order the CTAs finish in: the
+// kernel is bit-reproducible from run to run.
+//
 // Reference: RWKV7Base.decode and its per-token kernels (demo/_rwkv7_base.py:74-87,
 // 153-206, 276-292; src/rwkv_tl/kernels/{lerp,gates,dplr}.py) with the decode rounding
 // points -- the same arithmetic, in the same order, as the three-kernel path in
@@ -108,7 +112,7 @@ struct PParams {
   const __half *emb, *head, *lnout_w, *lnout_b;
   __half* logits;
   __half *xln1, *xln2, *rkv, *ranks, *vfirst;
-  float* acc;  // per layer: acc1 [B][C], then acc2 [NREP][B][C]
+  long long* acc;  // per layer, fixed point (fx_add): acc1 [B][C], then acc2 [NREP][B][C]
   GridBar* bar;
   float* rnn;
   __half *tmix_x, *cmix_x;
@@ -346,15 +350,17 @@ __device__ __forceinline__ void st4h(__half* p, const float (&v)[4]) {
 __device__ __forceinline__ void cp4h(__half* dst, const __half* src) {
   *reinterpret_cast<uint2*>(dst) = __ldcg(reinterpret_cast<const uint2*>(src));
 }
-// fp16(sum of the NREP accumulator replicas) of four channels, replicas in order.
-__device__ __forceinline__ void ld_acc_rep(const float* a, size_t rep_stride, float (&v)[4]) {
-  float4 s = __ldcg(reinterpret_cast<const float4*>(a));
+// fp16(sum of the NREP fixed-point accumulator replicas) of four channels.
+__device__ __forceinline__ void ld_acc_rep(const long long* a, size_t rep_stride, float (&v)[4]) {
+  long long s[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int r = 1; r < NREP; ++r) {
-    const float4 t = __ldcg(reinterpret_cast<const float4*>(a + r * rep_stride));
-    s.x += t.x; s.y += t.y; s.z += t.z; s.w += t.w;
+  for (int r = 0; r < NREP; ++r) {
+    const longlong2 t0 = __ldcg(reinterpret_cast<const longlong2*>(a + r * rep_stride));
+    const longlong2 t1 = __ldcg(reinterpret_cast<const longlong2*>(a + r * rep_stride + 2));
+    s[0] += t0.x; s[1] += t0.y; s[2] += t1.x; s[3] += t1.y;
   }
-  v[0] = r16(s.x); v[1] = r16(s.y); v[2] = r16(s.z); v[3] = r16(s.w);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = r16(fx_val(s[k]));
 }
 
 // Per-CTA staging state: one mbarrier per stream, and how many phases of each were
@@ -531,8 +537,8 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
 
   for (int l = 0; l < P.L && alive; ++l) {
     const DecLayer& Lw = P.layers[l];
-    float* acc1 = P.acc + (size_t)l * (1 + NREP) * BC;
-    float* acc2 = acc1 + BC;
+    long long* acc1 = P.acc + (size_t)l * (1 + NREP) * BC;
+    long long* acc2 = acc1 + BC;
     float* rnn = P.rnn + (size_t)l * P.n_slots * H * 4096;
     __half* tmix_x = P.tmix_x + (size_t)l * P.n_slots * C;
     __half* cmix_x = P.cmix_x + (size_t)l * P.n_slots * C;
@@ -540,7 +546,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
     // =================== phase A ===================
     {
       float lw[E] = {}, lb[E] = {}, mu[6][E] = {}, x[NB][E], prev[NB][E] = {};
-      const float* acc2p = acc1 - (size_t)NREP * BC;  // previous layer's FFN sums
+      const long long* acc2p = acc1 - (size_t)NREP * BC;  // previous layer's FFN sums
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         const int bb = b < B ? b : 0;
@@ -815,8 +821,9 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
         const int nq = (b_c1 - b_c0) / 4;  // whole quads of rows
         for (int i = tid; i < B * nq; i += NT) {
           const int n = i / nq, q = i % nq;
-          atomicAdd(reinterpret_cast<float4*>(acc1 + (size_t)n * C + b_c0 + 4 * q),
-                    *reinterpret_cast<const float4*>(pst + n * 128 + 4 * q));
+          const float4 v4 = *reinterpret_cast<const float4*>(pst + n * 128 + 4 * q);
+          long long* dst = acc1 + (size_t)n * C + b_c0 + 4 * q;
+          fx_add(dst, v4.x); fx_add(dst + 1, v4.y); fx_add(dst + 2, v4.z); fx_add(dst + 3, v4.w);
         }
       }
       if (jb == 0)  // new tmix state x (LN1 output) for this head's channels
@@ -854,12 +861,13 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
         const int bb = b < B ? b : 0;
         if (ew) {
           float xr[E];
-          const float4 a = __ldcg(reinterpret_cast<const float4*>(acc1 + (size_t)bb * C + c0));
+          const longlong2 a01 = __ldcg(reinterpret_cast<const longlong2*>(acc1 + (size_t)bb * C + c0));
+          const longlong2 a23 = __ldcg(reinterpret_cast<const longlong2*>(acc1 + (size_t)bb * C + c0 + 2));
           ld4h(sXr + (size_t)bb * C + c0, xr);
-          x[b][0] = r16(xr[0] + r16(a.x));
-          x[b][1] = r16(xr[1] + r16(a.y));
-          x[b][2] = r16(xr[2] + r16(a.z));
-          x[b][3] = r16(xr[3] + r16(a.w));
+          x[b][0] = r16(xr[0] + r16(fx_val(a01.x)));
+          x[b][1] = r16(xr[1] + r16(fx_val(a01.y)));
+          x[b][2] = r16(xr[2] + r16(fx_val(a23.x)));
+          x[b][3] = r16(xr[3] + r16(fx_val(a23.y)));
         } else {
 #pragma unroll
           for (int k = 0; k < E; ++k) x[b][k] = 0.f;
@@ -933,9 +941,8 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
           stage_tile<NB>(vst, C, 16 * (mt + 8), d[1], lane);
         }
         __syncthreads();
-        float* acc2r = acc2 + (size_t)(cta % NREP) * BC;
-        for (int i = tid; i < B * C / 4; i += NT)
-          atomicAdd(reinterpret_cast<float4*>(acc2r) + i, reinterpret_cast<const float4*>(vst)[i]);
+        long long* acc2r = acc2 + (size_t)(cta % NREP) * BC;
+        for (int i = tid; i < B * C; i += NT) fx_add(acc2r + i, vst[i]);
       }
       if (l + 1 == P.L) {  // the value slice is consumed: head tile 2 takes its place
         __syncthreads();
@@ -965,7 +972,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
   STAMP(250);
   {
     __half* xh = sXc;  // [NB][MLD]
-    const float* acc2 = P.acc + (size_t)(P.L - 1) * (1 + NREP) * BC + BC;
+    const long long* acc2 = P.acc + (size_t)(P.L - 1) * (1 + NREP) * BC + BC;
     __half* cmix_last = P.cmix_x + (size_t)(P.L - 1) * P.n_slots * C;
     float lw[E] = {}, lb[E] = {}, x[NB][E];
     if (ew) {
@@ -1148,7 +1155,7 @@ int check_model_public(const rwkv7_model* m);
 // barrier, laid out so one memset clears the accumulators and the barrier together.
 struct PersistWork {
   __half *xln1, *xln2, *rkv, *ranks, *vfirst;
-  float* acc;
+  long long* acc;
   GridBar* bar;
   size_t zero_bytes;
 };
@@ -1168,7 +1175,7 @@ static size_t carve_persist(void* base, PersistWork* w, int L, int B, int C) {
   d.ranks = (__half*)take((size_t)B * RWKV_RANK_SUM * 2);
   d.vfirst = (__half*)take(BC * 2);
   const size_t acc_off = off;
-  d.acc = (float*)take((size_t)L * (1 + NREP) * BC * 4);
+  d.acc = (long long*)take((size_t)L * (1 + NREP) * BC * 8);
   d.bar = (GridBar*)take(sizeof(GridBar));
   d.zero_bytes = off - acc_off;
   if (w) *w = d;
