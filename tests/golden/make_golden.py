@@ -16,6 +16,10 @@ format and loaded through the reference's ``RWKV7Weight``:
   same cases. On CPU the reference's fp16 kernels run their torch fallbacks
   (``src/rwkv_tl/kernels/*.py``, ``device.type != "cuda"`` branches), which round
   after every torch op, so this pins the fp16 oracle only loosely.
+* ``loader_bf16.pt`` -- the reference loader ``RWKV7Weight(path, device="cpu",
+  dtype=torch.float16)`` (``src/rwkv_tl/weight.py:155-184``) on a bf16 ``.pth`` file of
+  the tiny config (seed 3): the fp16 embedding with LN0 folded in, the head, ln_out and
+  every per-layer tensor in the reference's own orientation.
 * ``cfg0_torch_fp32.pt``: 0.1B (L=12, C=768, V=65536,
   seed 0), 8-token prompt of seeded uniform ids, ``forward`` then 16 greedy
   decode steps with ``RWKV7Torch`` in fp32. Stores the generated tokens, the
@@ -98,6 +102,26 @@ def main() -> None:
         out["tokens"] = torch.tensor(TINY_TOKENS)
         out["how"] = "RWKV7FP16 (CPU torch fallbacks), CONFIG_TINY seed 1"
         torch.save(out, HERE / "tiny_fp16_cpu.pt")
+
+        # ---- loader: a bf16 checkpoint file through the reference's RWKV7Weight ----
+        p = os.path.join(td, "tiny_bf16.pth")
+        torch.save(synth_checkpoint(CONFIG_TINY, seed=3, dtype=torch.bfloat16), p)
+        wr = RWKV7Weight(p, device="cpu", dtype=torch.float16)
+        blocks = []
+        for b in wr.blocks:
+            a, f = b.att, b.ffn
+            blocks.append({
+                "ln1": (b.att.ln_pre.w, b.att.ln_pre.b), "ln2": (f.ln_pre.w, f.ln_pre.b),
+                "ln_x": (a.ln_x.w, a.ln_x.b),
+                **{n: getattr(a, n) for n in ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g", "w0",
+                                              "w1", "w2", "a0", "a1", "a2", "v0", "v1", "v2",
+                                              "g1", "g2", "r_k", "k_k", "k_a", "rkvWt", "oWt")},
+                "ffn_x_k": f.x_k, "kWt": f.kWt, "vWt": f.vWt,
+            })
+        torch.save({"emb": wr.emb, "head": wr.head, "ln_out": (wr.ln_out.w, wr.ln_out.b),
+                    "blocks": blocks,
+                    "how": "reference RWKV7Weight(tiny bf16 .pth, cpu, fp16), CONFIG_TINY seed 3"},
+                   HERE / "loader_bf16.pt")
 
         # ---- config 0: 0.1B fp32 pure torch, 8-token prompt + 16 greedy steps ----
         p = os.path.join(td, "cfg0.pth")

@@ -77,3 +77,41 @@ def test_synth_checkpoint_keys_and_init():
     assert w0.min() >= -6 and w0.max() <= -1
     assert torch.equal(sd["blocks.0.att.k_a"], torch.ones(1, 1, 128))
     assert torch.equal(synth_checkpoint(CONFIG_TINY, seed=0)["head.weight"], sd["head.weight"])
+
+
+def test_loader_bf16_pth_matches_reference_loader(tmp_path):
+    """A bf16 ``.pth`` file through ``RWKV7Weight`` gives the tensors the reference's own
+    loader gives (``src/rwkv_tl/weight.py:155-184``, fixture ``loader_bf16.pt`` made by
+    running it): every cast and re-layout bit-exact, the LN0-folded embedding to within
+    one fp16 rounding (fp32 reduction order of the LayerNorm)."""
+    import torch
+
+    from rwkv_tl_b200.synth import CONFIG_TINY, synth_checkpoint
+    from rwkv_tl_b200.weight import RWKV7Weight
+    from tests.conftest import GOLDEN
+
+    ref = torch.load(GOLDEN / "loader_bf16.pt", weights_only=False)
+    p = tmp_path / "tiny_bf16.pth"
+    torch.save(synth_checkpoint(CONFIG_TINY, seed=3, dtype=torch.bfloat16), p)
+    w = RWKV7Weight(str(p), device="cpu")
+    assert w.emb.dtype == torch.float16 and w.L == len(ref["blocks"])
+    d = (w.emb.float() - ref["emb"].float()).abs()
+    ulp = torch.finfo(torch.float16).eps * ref["emb"].float().abs().clamp(min=2 ** -14)
+    assert bool((d <= ulp).all()) and float((d > 0).float().mean()) < 0.01
+    assert torch.equal(w.head, ref["head"])
+    assert torch.equal(w.lnout_w, ref["ln_out"][0]) and torch.equal(w.lnout_b, ref["ln_out"][1])
+    for lay, rb in zip(w.layers, ref["blocks"]):
+        eq = lambda a, b: torch.equal(a, b.reshape(a.shape))  # noqa: E731
+        assert eq(lay["w_rkv"], torch.cat([rb["rkvWt"][i].t() for i in range(3)], 0))
+        assert eq(lay["w_o"], rb["oWt"].t()) and eq(lay["w_fk"], rb["kWt"].t())
+        assert eq(lay["w_fv"], rb["vWt"].t())
+        assert eq(lay["w_lora_dn"], torch.cat([rb[g + "1"].t() for g in "vwag"], 0))
+        assert eq(lay["w_lora_up"], torch.cat([rb[g + "2"] for g in "vwag"], 0))
+        assert eq(lay["mix6"], torch.stack([rb[n].reshape(-1) for n in
+                                            ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")]))
+        for ours, theirs in (("w0", "w0"), ("a0", "a0"), ("v0", "v0"), ("k_k", "k_k"),
+                             ("k_a", "k_a"), ("r_k", "r_k"), ("ffn_x_k", "ffn_x_k")):
+            assert eq(lay[ours], rb[theirs])
+        for ours, theirs in (("ln1_w", ("ln1", 0)), ("ln1_b", ("ln1", 1)), ("ln2_w", ("ln2", 0)),
+                             ("ln2_b", ("ln2", 1)), ("lnx_w", ("ln_x", 0)), ("lnx_b", ("ln_x", 1))):
+            assert eq(lay[ours], rb[theirs[0]][theirs[1]])
