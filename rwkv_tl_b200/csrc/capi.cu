@@ -54,6 +54,12 @@ bool rwkv_chain_take_pdl() {
   return !first && rwkv_pdl_enabled();
 }
 
+bool rwkv_rows_wide(int M, int C) {
+  const char* e = getenv("RWKV_B200_NARROW");
+  if (e && e[0] == '1') return false;
+  return M >= 1024 && C % 256 == 0;
+}
+
 int decode_persist_timeout_flag();
 int wkv_chunk_bad_flag();
 extern "C" int rwkv_b200_device_error(void) {

@@ -169,6 +169,10 @@ struct PendingResid {
   int splits;
 };
 
+// Large token batches (M >= 1024) run the row, gate and GroupNorm kernels with 8
+// channels per thread; RWKV_B200_NARROW=1 keeps the narrow layouts at every size
+// (their sums replay the same summation trees, so results are bit-identical).
+bool rwkv_rows_wide(int M, int C);
 bool rwkv_pdl_enabled();  // RWKV_B200_PDL=0 turns the attribute off (plain stream order)
 // Start of a library call: its first launch depends on whatever the caller queued
 // before (copies, memsets, other libraries' kernels) in plain stream order; only

@@ -181,7 +181,7 @@ __global__ void k_gates_ew(
 int launch_gates_ew(int sem, const void* lora, const __half* rkv, const __half* w0,
                     const __half* a0, const __half* v0, const __half* k_k, const __half* k_a,
                     __half* vfirst, __half* gout, int M, int C, int layer0, cudaStream_t st) {
-  const bool wide = M >= 1024;  // 8 channels per lane once the grid is large
+  const bool wide = rwkv_rows_wide(M, 256);  // 8 channels per lane once the grid is large
   const int lanes = ((C / (wide ? 8 : 2) + 31) / 32) * 32;
   const int threads = lanes < 256 ? lanes : 256;
   const dim3 grid(M, (lanes + threads - 1) / threads), block(threads);

@@ -299,7 +299,7 @@ __global__ void k_scatter_state_x(const __half* __restrict__ xlast, __half* __re
 }
 
 // 8 channels per thread once the batch is large (and C / 8 is whole warps).
-static bool rows_wide(int M, int C) { return M >= 1024 && C % 256 == 0; }
+static bool rows_wide(int M, int C) { return rwkv_rows_wide(M, C); }
 
 int launch_tmix_rows(int sem, __half* x, const int64_t* tokens, const __half* emb,
                      const __half* ln_w, const __half* ln_b, const __half* mix6,

@@ -1056,7 +1056,7 @@ int launch_wkv_epilogue(int sem, const __half* ybuf, const __half* rbuf, const _
                         size_t plane, const __half* r_k, const __half* lnx_w,
                         const __half* lnx_b, __half* yg, int M, int C, cudaStream_t st) {
   // 8 channels per thread on large batches (C / 8 whole warps)
-  const bool wide = M >= 1024 && C % 256 == 0;
+  const bool wide = rwkv_rows_wide(M, C);
 #define EPI_GO(S, V)                                                                           \
   return rwkv_launch("wkv_epilogue", k_wkv_epilogue<S, V>, dim3(M), dim3(C / V), 0, st, ybuf, \
                      rbuf, gbuf, plane, r_k, lnx_w, lnx_b, yg, C)

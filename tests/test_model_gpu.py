@@ -364,3 +364,22 @@ def test_small_batch_decode_is_bit_reproducible(monkeypatch, B, mode):
     for o in outs[1:]:
         for a, b in zip(outs[0], o):
             assert torch.equal(a, b)
+
+
+def test_wide_and_narrow_row_layouts_are_bit_identical(monkeypatch):
+    """Token batches of >= 1024 rows run the row / gate / GroupNorm kernels 8 channels
+    per thread; their sums replay the narrow layouts' summation trees, so forcing the
+    narrow layouts (RWKV_B200_NARROW=1) changes no bit of the states or the logits."""
+    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 7)
+    seqs = [torch.tensor(_tokens(n, 4096, 60 + i)) for i, n in enumerate((900, 700, 400))]
+    toks = torch.tensor(_tokens(1100, 4096, 70), device="cuda")
+    out = {}
+    for mode in ("wide", "narrow"):
+        monkeypatch.setenv("RWKV_B200_NARROW", "1" if mode == "narrow" else "0")
+        bs = BatchedState(m.L, m.C, 1100, device="cuda")
+        m.prefill_batch(seqs, bs)
+        lg = m.decode_batch(toks, bs)
+        torch.cuda.synchronize()
+        out[mode] = (bs.rnn.clone(), bs.tmix_x.clone(), bs.cmix_x.clone(), lg.clone())
+    for a, b in zip(out["wide"], out["narrow"]):
+        assert torch.equal(a, b)
