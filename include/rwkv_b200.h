@@ -199,6 +199,19 @@ int rwkv7_dplr_chunked_noalloc(void* S, const void* r, const void* w, const void
                                const void* v, const void* a, const void* b, void* y, int n_seq,
                                int T, int H, void* stream);
 
+/* Token sampling, one kernel for B rows of fp16 logits [B, V] (V <= 65536, a multiple
+ * of 8, logits 16-byte aligned): repetition penalty on each row's seen ids (CSR:
+ * seen[seen_cu[b] .. seen_cu[b+1]); NULL for none), then greedy argmax (lowest id on
+ * ties) when temperature <= 0; else logits / temperature, top-k (0 = off; ties with
+ * the k-th logit kept), nucleus top-p (1 = off; a token is kept when the mass ranked
+ * above it is <= top_p) and one draw per row from the kept softmax at the caller's
+ * uniform uniforms[b] in [0, 1). out: int64 [B]. Replaces sample_logits
+ * (demo/sampling.py:13-70): same rules, same distribution; ids differ from
+ * torch.multinomial's for the same seed. Bit-reproducible for fixed inputs. */
+int rwkv7_sample(const void* logits, int B, int V, float temperature, int top_k, float top_p,
+                 float repetition_penalty, const int64_t* seen, const int* seen_cu,
+                 const float* uniforms, int64_t* out, void* stream);
+
 /* Grouped fp16 GEMM, up to 4 independent problems in one launch:
  *   C_g[M_g, N_g] = epi( A_g[M_g, K_g] @ B_g[N_g, K_g]^T )
  * A row-major (lda), B row-major [N, K] (ldb), C/R row-major (ldc). K_g must be

@@ -27,6 +27,7 @@ EXPORTED = (
     "rwkv7_dplr_chunked",
     "rwkv7_dplr_chunked_noalloc",
     "rwkv7_gemm_f16",
+    "rwkv7_sample",
     "rwkv7_forward_workspace_bytes",
     "rwkv7_forward",
     "rwkv7_decode_gemv_workspace_bytes",
@@ -118,6 +119,9 @@ def load() -> C.CDLL:
     lib.rwkv7_dplr_chunked_noalloc.argtypes = [vp] * 8 + [C.c_int] * 3 + [vp]
     lib.rwkv7_wkv_gn_step.restype = C.c_int
     lib.rwkv7_wkv_gn_step.argtypes = [vp] * 13 + [C.c_int, C.c_int, C.c_int, vp]
+    lib.rwkv7_sample.restype = C.c_int
+    lib.rwkv7_sample.argtypes = [vp, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float,
+                                 vp, vp, vp, vp, vp]
     lib.rwkv7_gemm_f16.restype = C.c_int
     lib.rwkv7_gemm_f16.argtypes = [C.POINTER(GemmProblem), C.c_int, C.c_int, vp]
     lib.rwkv7_forward_workspace_bytes.restype = C.c_size_t
