@@ -859,6 +859,10 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_
     while (splits > 1 && (size_t)splits * mn > ws_floats) --splits;
   }
   if (splits_out) *splits_out = splits;
+  // more 128 x 64 tiles than SMs (the prefill LoRA-down): 3 stages (72 KiB) let two or
+  // three CTAs share an SM, so the grid runs as one wave instead of two
+  if (splits == 1 && tiles64 > device_sm_count())
+    return gemm_tc_launch_cfg<64, 3>(p, n, epi, 1, ws, false, st);
   return gemm_tc_launch_cfg<64, 6>(p, n, epi, splits, ws, splits_out != nullptr, st);
 }
 
