@@ -1,4 +1,4 @@
-// Small-batch decode (one token for each of B <= 2 sequences; B = 3, 4 as two launches)
+// Small-batch decode (one token for each of B <= 4 sequences; layouts for 1, 2 and 4)
 // as ONE persistent kernel per step: one CTA per SM, launched cooperatively so that
 // every CTA is resident, with a grid barrier between the three phases of each layer
 // and before the head.
@@ -129,17 +129,25 @@ struct SmemLayout {
 __host__ __device__ inline size_t al1k(size_t v) { return (v + 1023) & ~size_t(1023); }
 __host__ __device__ inline int mld_of(int C) { return C + 8; }  // padded activation rows
 
+// The sequences' token-shift rows (tmix x for phase A, cmix x for phase C) are staged
+// in shared memory with the other vectors for NB <= 2; the four-sequence layout reads
+// them from L2 (prefetched one phase ahead) to fit in 227 KB.
+__host__ __device__ constexpr int staged_x_rows(int NB) { return NB <= 2 ? NB : 0; }
+
 __host__ __device__ inline SmemLayout smem_layout(int NB, int C, int rows_b) {
   SmemLayout s;
   s.a = 0;
   s.ac = al1k(s.a + (size_t)RA * C * 2);
-  s.bv = al1k(s.ac + (size_t)(8 + NB) * C * 2);
+  s.bv = al1k(s.ac + (size_t)(8 + staged_x_rows(NB)) * C * 2);
   const size_t b_bytes = (size_t)RWKV_RANK_SUM * 128 + al1k((size_t)rows_b * 128);
   const size_t v_bytes = (size_t)C * 64;
   s.bc = al1k(s.bv + (b_bytes > v_bytes ? b_bytes : v_bytes));
   s.k = al1k(s.bc + 8 * 128);
   s.cc = al1k(s.k + (size_t)FROWS * C * 2);
-  s.xc = al1k(s.cc + (size_t)(3 + NB) * C * 2);
+  // for NB <= 2 the C-vector region doubles as the [NB][C] fp32 staging of the FFN
+  // value sums ((3 + NB) C halves >= NB C floats); four sequences stage them in the
+  // consumed FFN key rows
+  s.xc = al1k(s.cc + (size_t)(3 + staged_x_rows(NB)) * C * 2);
   s.xr = al1k(s.xc + (size_t)NB * mld_of(C) * 2);
   s.total = al1k(s.xr + (size_t)NB * C * 2);
   return s;
@@ -347,6 +355,12 @@ __device__ __forceinline__ void st4h(__half* p, const float (&v)[4]) {
   *reinterpret_cast<__half2*>(&u.y) = __floats2half2_rn(v[2], v[3]);
   *reinterpret_cast<uint2*>(p) = u;
 }
+__device__ __forceinline__ void ldcg4h(const __half* p, float (&v)[4]) {
+  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
 __device__ __forceinline__ void cp4h(__half* dst, const __half* src) {
   *reinterpret_cast<uint2*>(dst) = __ldcg(reinterpret_cast<const uint2*>(src));
 }
@@ -393,7 +407,7 @@ __device__ __forceinline__ void stage_a(const PParams& P, const DecLayer& L, con
   const int C = P.C;
   const uint32_t row = (uint32_t)C * 2;
   const bool task = cta < P.n_atask;
-  mbar_expect_tx(mb, (task ? (uint32_t)RA * row : 0u) + (uint32_t)(8 + NB) * row);
+  mbar_expect_tx(mb, (task ? (uint32_t)RA * row : 0u) + (uint32_t)(8 + staged_x_rows(NB)) * row);
   if (task) {
     const ATask t = P.atask[cta];
     tma_3d(sA, t.src == 0 ? &M.w_rkv : &M.lora_dn, 0, t.row0, 0, mb);
@@ -401,7 +415,9 @@ __device__ __forceinline__ void stage_a(const PParams& P, const DecLayer& L, con
   bulk_g2s(sAc, L.ln1_w, row, mb);
   bulk_g2s(sAc + C, L.ln1_b, row, mb);
   bulk_g2s(sAc + 2 * C, L.mix6, 6 * row, mb);
-  for (int b = 0; b < NB; ++b) bulk_g2s(sAc + (size_t)(8 + b) * C, tmix_x + (size_t)s_slot[b] * C, row, mb);
+  for (int b = 0; b < staged_x_rows(NB); ++b)
+    bulk_g2s(sAc + (size_t)(8 + b) * C, tmix_x + (size_t)s_slot[b] * C, row, mb);
+  for (int b = staged_x_rows(NB); b < NB; ++b) l2_prefetch_bulk(tmix_x + (size_t)s_slot[b] * C, row);
 }
 
 // Phase B: the head's LoRA-up slice [288][64], the CTA's rows of W_o[:, head] (both
@@ -435,12 +451,14 @@ __device__ __forceinline__ void stage_k(const PParams& P, const DecLayer& L, con
                                         __half* sFk, __half* sCc, int j0, uint64_t* mb) {
   const int C = P.C;
   const uint32_t row = (uint32_t)C * 2;
-  mbar_expect_tx(mb, (uint32_t)FROWS * row + (uint32_t)(3 + NB) * row);
+  mbar_expect_tx(mb, (uint32_t)FROWS * row + (uint32_t)(3 + staged_x_rows(NB)) * row);
   tma_3d(sFk, &M.w_fk, 0, j0, 0, mb);
   bulk_g2s(sCc, L.ln2_w, row, mb);
   bulk_g2s(sCc + C, L.ln2_b, row, mb);
   bulk_g2s(sCc + 2 * C, L.ffn_x_k, row, mb);
-  for (int b = 0; b < NB; ++b) bulk_g2s(sCc + (size_t)(3 + b) * C, cmix_x + (size_t)s_slot[b] * C, row, mb);
+  for (int b = 0; b < staged_x_rows(NB); ++b)
+    bulk_g2s(sCc + (size_t)(3 + b) * C, cmix_x + (size_t)s_slot[b] * C, row, mb);
+  for (int b = staged_x_rows(NB); b < NB; ++b) l2_prefetch_bulk(cmix_x + (size_t)s_slot[b] * C, row);
 }
 
 // Phase C: the FFN value slice W_fv[:, j0 : j0 + 32] as [C][32] (64-byte swizzle;
@@ -563,6 +581,9 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
           for (int k = 0; k < E; ++k) x[b][k] = r16(xr[k] + a[k]);
         }
       }
+      if (ew)  // unstaged token-shift rows (four-sequence layout), L2-prefetched
+        for (int b = staged_x_rows(NB); b < NB; ++b)
+          ldcg4h(tmix_x + (size_t)s_slot[b] * C + c0, prev[b]);
       if (l == 10) STAMP(200);
       if (!stage_wait(S, MB_A, P.bar)) { alive = false; break; }
       if (l == 10) STAMP(201);
@@ -573,7 +594,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
         for (int t = 0; t < 6; ++t) ld4h(sAc + (2 + t) * C + c0, mu[t]);
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-          ld4h(sAc + (8 + b) * C + c0, prev[b]);
+          if (b < staged_x_rows(NB)) ld4h(sAc + (8 + b) * C + c0, prev[b]);
           st4h(sXr + (size_t)b * C + c0, x[b]);  // this layer's input, kept for phase C
         }
         if (cta == 0 && l > 0)  // previous layer's cmix state x (read there by every CTA)
@@ -873,6 +894,9 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
           for (int k = 0; k < E; ++k) x[b][k] = 0.f;
         }
       }
+      if (ew)
+        for (int b = staged_x_rows(NB); b < NB; ++b)
+          ldcg4h(cmix_x + (size_t)s_slot[b] * C + c0, prev[b]);
       if (l == 10) STAMP(151);
       if (!stage_wait(S, MB_K, P.bar)) { alive = false; break; }
       if (l == 10) STAMP(152);
@@ -882,7 +906,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
         ld4h(sCc + 2 * C + c0, mu);
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-          ld4h(sCc + (3 + b) * C + c0, prev[b]);
+          if (b < staged_x_rows(NB)) ld4h(sCc + (3 + b) * C + c0, prev[b]);
           st4h(sXr + (size_t)b * C + c0, x[b]);  // x1, the next layer's residual
         }
       }
@@ -910,7 +934,7 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
         hh[n * HLD + j] = f2h(j < f_nj ? r16(hv * hv) : 0.f);
       }
       __syncthreads();
-      if (l + 1 == P.L) {  // key rows consumed: head tile 1 takes their place
+      if (NB <= 2 && l + 1 == P.L) {  // key rows consumed: head tile 1 takes their place
         if (tid == 0) stage_head(P, 1, v0, v1, head_slot(1), &s_mb[MB_H1]);
         ++S.issued[MB_H1];
       }
@@ -921,7 +945,9 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
          // takes the 16-row tiles w, w + 8, ...; the slice has a 64-byte swizzle (16-byte
          // chunk q of row c at q ^ ((c / 2) % 4))
         const uint32_t vb = saddr(sV);
-        float* vst = reinterpret_cast<float*>(sCc);  // [NB][C] staging (C vectors consumed)
+        // [NB][C] fp32 staging of the sums: the consumed C vectors, or for four sequences
+        // (which do not fit there) the consumed FFN key rows
+        float* vst = reinterpret_cast<float*>(NB <= 2 ? sCc : sFk);
         uint32_t hb0[2], hb1[2];
         b_frag<NB>(hh, HLD, 0, lane, hb0[0], hb1[0]);
         b_frag<NB>(hh, HLD, 16, lane, hb0[1], hb1[1]);
@@ -946,7 +972,12 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
       }
       if (l + 1 == P.L) {  // the value slice is consumed: head tile 2 takes its place
         __syncthreads();
-        if (tid == 0) stage_head(P, 2, v0, v1, head_slot(2), &s_mb[MB_H2]);
+        if (tid == 0) {
+          // four sequences: the key rows held the staged sums until now
+          if (NB > 2) stage_head(P, 1, v0, v1, head_slot(1), &s_mb[MB_H1]);
+          stage_head(P, 2, v0, v1, head_slot(2), &s_mb[MB_H2]);
+        }
+        if (NB > 2) ++S.issued[MB_H1];
         ++S.issued[MB_H2];
       }
     }
@@ -1206,7 +1237,7 @@ bool decode_persist_supported(const rwkv7_model* m, int B, const rwkv7_state* st
   ATask tmp[MAXG];
   if (build_atasks(C, tmp, MAXG) > G) return false;
   if ((4 * C / 8 + G - 1) / G > FROWS / 8) return false;
-  const int NB = B == 1 ? 1 : 2;  // B = 3, 4 run as two launches of <= 2 sequences
+  const int NB = B <= 2 ? B : 4;
   const size_t smem = smem_layout(NB, C, rows_b_of(C, G)).total;
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
@@ -1293,24 +1324,17 @@ static int run_persist(const rwkv7_model* m, const int64_t* tokens, int B, const
   return rwkv_check_launch("decode_persist");
 }
 
-// B <= 2 in one launch; B = 3, 4 as two launches of <= 2 sequences (the two-sequence
-// layout is the largest that fits shared memory, and two of its steps beat one step of
-// the three-kernel path).
+// One launch: the one-, two- or four-sequence layout (B = 3 runs the four-sequence
+// layout with one column idle).
 int decode_persist_run(const rwkv7_model* m, const int64_t* tokens, int B, const int* slots,
                        const rwkv7_state* state, void* logits, void* ws, cudaStream_t st) {
   const bool c768 = m->n_embd == 768;
-  auto one = [&](int off, int nb) {
-    const int64_t* t = tokens + off;
-    const int* sl = slots ? slots + off : nullptr;
-    void* lg = static_cast<__half*>(logits) + (size_t)off * m->vocab;
-    if (nb == 1) return c768 ? run_persist<1, 3>(m, t, 1, sl, off, state, lg, ws, st)
-                             : run_persist<1, 4>(m, t, 1, sl, off, state, lg, ws, st);
-    return c768 ? run_persist<2, 3>(m, t, nb, sl, off, state, lg, ws, st)
-                : run_persist<2, 4>(m, t, nb, sl, off, state, lg, ws, st);
-  };
-  if (B <= 2) return one(0, B);
-  const int rc = one(0, 2);
-  return rc ? rc : one(2, B - 2);
+  if (B == 1) return c768 ? run_persist<1, 3>(m, tokens, 1, slots, 0, state, logits, ws, st)
+                          : run_persist<1, 4>(m, tokens, 1, slots, 0, state, logits, ws, st);
+  if (B == 2) return c768 ? run_persist<2, 3>(m, tokens, 2, slots, 0, state, logits, ws, st)
+                          : run_persist<2, 4>(m, tokens, 2, slots, 0, state, logits, ws, st);
+  return c768 ? run_persist<4, 3>(m, tokens, B, slots, 0, state, logits, ws, st)
+              : run_persist<4, 4>(m, tokens, B, slots, 0, state, logits, ws, st);
 }
 
 #if PERSIST_STAMPS
