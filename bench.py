@@ -53,7 +53,12 @@ def peaks() -> tuple[dict, str]:
 
 
 class Clocks:
-    """Sample nvidia-smi clocks / throttle reasons while the timed region runs."""
+    """Sample nvidia-smi clocks / throttle reasons while the timed region runs.
+
+    The sampler is started, and its first sample awaited (up to 5 s), before the
+    caller's timed region begins; ``mark()`` brackets the timed region, and the summary
+    uses the samples taken inside it (the closest ones when the region is shorter
+    than the 50 ms sampling period)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -62,8 +67,17 @@ class Clocks:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.lines: list = []
+        self.window = [None, None]
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.lines.append((time.time(), ln))
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
@@ -71,23 +85,36 @@ class Clocks:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        threading.Thread(target=self._read, daemon=True).start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0:
+            time.sleep(0.01)
         return self
 
+    def mark(self, which: int) -> None:
+        self.window[which] = time.time()
+
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
+            time.sleep(0.06)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self) -> dict:
         sm, smax, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        t0, t1 = self.window
+        lines = list(self.lines)
+        if t0 is not None and t1 is not None:
+            inside = [x for x in lines if t0 <= x[0] <= t1 + 0.05]
+            if not inside and lines:  # region shorter than one sampling period
+                inside = [min(lines, key=lambda x: abs(x[0] - (t0 + t1) / 2))]
+            lines = inside
+        for _, ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -253,7 +280,10 @@ def run_b200(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     with Clocks(local) as clk:
+        barrier(world)
+        clk.mark(0)
         ms = timed(step, args.steps, stream)
+        clk.mark(1)
         barrier(world)
     ms = max_over_ranks(ms, world)
     value = world * B / (ms * 1e-3)
