@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_gemm_tc(const __grid_constant__
     grid_dep_wait();
     return;
   }
-  const int KB = P.K / BK;
+  const int KB = (P.K + BK - 1) / BK;  // a partial last K-block reads zeros past K (TMA fill)
   const int kb_per = (KB + prm.splits - 1) / prm.splits;
   const int kb0 = split * kb_per, kb1 = min(KB, kb0 + kb_per);
   // a K-slice past the end still writes its (zero) partial tile for the reduce
@@ -559,7 +559,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int g, m0, n0;
         tile_of(prm, tm, t, g, m0, n0);
-        const int nk = prm.p[g].K / BK;
+        const int nk = (prm.p[g].K + BK - 1) / BK;
         // the first tile's weight stages go out before the programmatic wait
         int pre = 0;
         if (!waited) {
@@ -607,7 +607,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++j) {
         int g, m0, n0;
         tile_of(prm, tm, t, g, m0, n0);
-        const int nk = prm.p[g].K / BK;
+        const int nk = (prm.p[g].K + BK - 1) / BK;
         const int b = j & 1;
         const uint32_t u = (uint32_t)(j >> 1);
         // accumulator b must have been drained by the epilogue of its previous tile
@@ -754,16 +754,6 @@ int launch_tc_persist(const TcParams& prm, const TileMap& tm, cudaStream_t st) {
 }  // namespace
 
 // True when every problem fits the tcgen05 path (K multiple of 64, aligned operands).
-bool gemm_tc_eligible(const rwkv7_gemm_problem* p, int n) {
-  for (int i = 0; i < n; ++i) {
-    if (p[i].K % BK || p[i].lda % 8 || p[i].ldb % 8 || p[i].M <= 0 || p[i].N <= 0) return false;
-    if ((reinterpret_cast<uintptr_t>(p[i].A) | reinterpret_cast<uintptr_t>(p[i].B)) & 15)
-      return false;
-    if ((reinterpret_cast<uintptr_t>(p[i].C) | reinterpret_cast<uintptr_t>(p[i].R)) & 7) return false;
-  }
-  return true;
-}
-
 template <int BN, int STAGES>
 int gemm_tc_launch_cfg(const rwkv7_gemm_problem* p, int n, int epi, int splits, float* ws,
                        bool defer, cudaStream_t st);
@@ -840,7 +830,7 @@ int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_
   for (int i = 0; i < n; ++i) {
     tiles128 += ((p[i].M + BM - 1) / BM) * ((p[i].N + 127) / 128);
     tiles64 += ((p[i].M + BM - 1) / BM) * ((p[i].N + 63) / 64);
-    min_kb = min(min_kb, p[i].K / BK);
+    min_kb = min(min_kb, (p[i].K + BK - 1) / BK);
     mn += (size_t)p[i].M * p[i].N;
     n4 = n4 && p[i].N % 4 == 0 && p[i].ldc % 2 == 0;
   }
@@ -949,4 +939,54 @@ int gemm_tc_timeout_flag() {
     cudaMemcpyToSymbol(g_tc_timeout, &z, sizeof(int));
   }
   return v;
+}
+
+// ---- public GEMM entry ------------------------------------------------------
+// Validation of a group of up to 4 problems (shapes, strides, alignment).
+int gemm_validate(const rwkv7_gemm_problem* p, int n) {
+  if (!p || n < 1 || n > 4) {
+    rwkv_set_error("rwkv7_gemm_f16: need 1..4 problems (got %d)", n);
+    return RWKV_ERR_ARG;
+  }
+  for (int i = 0; i < n; ++i) {
+    const rwkv7_gemm_problem& q = p[i];
+    if (q.M < 0 || q.N < 0 || q.K <= 0 || q.K % 32 || q.N % 2 || q.lda % 8 || q.ldb % 8 ||
+        q.ldc % 2 || !q.A || !q.B || !q.C || (reinterpret_cast<uintptr_t>(q.C) & 7) ||
+        (reinterpret_cast<uintptr_t>(q.R) & 7) || q.lda < q.K || q.ldb < q.K || q.ldc < q.N) {
+      rwkv_set_error("rwkv7_gemm_f16: bad problem %d (M=%d N=%d K=%d lda=%d ldb=%d ldc=%d)", i,
+                     q.M, q.N, q.K, q.lda, q.ldb, q.ldc);
+      return RWKV_ERR_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(q.A) | reinterpret_cast<uintptr_t>(q.B)) & 15) {
+      rwkv_set_error("rwkv7_gemm_f16: A and B must be 16-byte aligned (problem %d)", i);
+      return RWKV_ERR_ARG;
+    }
+  }
+  return RWKV_OK;
+}
+
+// Every GEMM runs on the tcgen05 kernels (K % 64 == 32 included: the last K-block's
+// tensor-map box reaches past K and the TMA fills it with zeros). `ws` is the split-K
+// scratch; with `splits_out` non-null a split-K GEMM leaves its fp32 K-slices in ws for
+// the consumer to sum (*splits_out > 1) instead of launching the reduce.
+int gemm_launch_ws(const rwkv7_gemm_problem* problems, int n, int epi, float* ws,
+                   size_t ws_floats, cudaStream_t st, int* splits_out) {
+  return gemm_tc_launch(problems, n, epi, ws, ws_floats, st, splits_out);
+}
+
+extern "C" int rwkv7_gemm_f16(const rwkv7_gemm_problem* problems, int n_problems, int epilogue,
+                              void* stream) {
+  rwkv_chain_begin();
+  int rc = gemm_validate(problems, n_problems);
+  if (rc) return rc;
+  if (epilogue < RWKV_EPI_STORE || epilogue > RWKV_EPI_LORA_ACT2) {
+    rwkv_set_error("rwkv7_gemm_f16: unknown epilogue %d", epilogue);
+    return RWKV_ERR_ARG;
+  }
+  for (int i = 0; i < n_problems; ++i)
+    if (epilogue == RWKV_EPI_RESID && !problems[i].R) {
+      rwkv_set_error("rwkv7_gemm_f16: residual epilogue needs R (problem %d)", i);
+      return RWKV_ERR_ARG;
+    }
+  return gemm_launch_ws(problems, n_problems, epilogue, nullptr, 0, (cudaStream_t)stream, nullptr);
 }
