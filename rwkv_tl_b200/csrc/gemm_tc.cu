@@ -511,6 +511,76 @@ __device__ __forceinline__ void tile_of(const TcParams& prm, const TileMap& tm, 
   n0 = (local / tm.tiles_m[g]) * PBN;
 }
 
+// Epilogue of one 128-row x PBN-column accumulator slice (TMEM lanes quad*32.., columns
+// from trow): thread `row` of the output drains its TMEM lane through the fused epilogue.
+template <int EPI>
+__device__ __forceinline__ void persist_epilogue(const TcProblem& P, int g, int row, int n0,
+                                                 uint32_t trow) {
+  void* C = P.C;
+  const __half* R = static_cast<const __half*>(P.R);
+  if constexpr (EPI == EPI_ARGMAX) {
+    unsigned long long best = 0;
+#pragma unroll 1
+    for (int c0 = 0; c0 < PBN; c0 += 16) {
+      float v[16];
+      tmem_ld16(trow + c0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int col = n0 + c0 + i;
+        if (col < P.N) {
+          const unsigned long long key = argmax_key(r16(v[i]), col);
+          best = key > best ? key : best;
+        }
+      }
+    }
+    if (row < P.M) atomicMax(static_cast<unsigned long long*>(C) + row, best);
+  } else {
+    const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(R) & 15) == 0;
+    if (EPI == RWKV_EPI_RESID && vec && n0 + PBN <= P.N) {
+      // residual rows: fetch the thread's whole 128-column slice first, so the tile
+      // pays one memory latency per half instead of one per 16 columns
+#pragma unroll 1
+      for (int h0 = 0; h0 < PBN; h0 += 128) {
+        uint4 rr[16];
+        const __half* rp = R + (size_t)row * P.ldc + n0 + h0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          rr[i] = row < P.M ? *reinterpret_cast<const uint4*>(rp + 8 * i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int c1 = 0; c1 < 128; c1 += 16) {
+          float v[16];
+          tmem_ld16(trow + h0 + c1, v);
+          if (row < P.M) {
+            uint4 pk[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const __half2* r2 = reinterpret_cast<const __half2*>(&rr[c1 / 8 + q]);
+              __half2* o2 = reinterpret_cast<__half2*>(&pk[q]);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 rf = __half22float2(r2[e]);
+                o2[e] = __floats2half2_rn(rf.x + r16(v[8 * q + 2 * e]), rf.y + r16(v[8 * q + 2 * e + 1]));
+              }
+            }
+            __half* cp = static_cast<__half*>(C) + (size_t)row * P.ldc + n0 + h0 + c1;
+            reinterpret_cast<uint4*>(cp)[0] = pk[0];
+            reinterpret_cast<uint4*>(cp)[1] = pk[1];
+          }
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int c0 = 0; c0 < PBN; c0 += 16) {
+        float v[16];
+        tmem_ld16(trow + c0, v);
+        const int col = n0 + c0;
+        if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec, g);
+      }
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_gemm_tc_persist(const __grid_constant__ TcParams prm, const __grid_constant__ TileMap tm) {
@@ -646,71 +716,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       int g, m0, n0;
       tile_of(prm, tm, t, g, m0, n0);
       const TcProblem& P = prm.p[g];
-      const int row = m0 + quad * 32 + lane;
-      const uint32_t trow = tmem + (uint32_t)(b * PBN) + ((uint32_t)(quad * 32) << 16);
-      void* C = P.C;
-      const __half* R = static_cast<const __half*>(P.R);
-      if constexpr (EPI == EPI_ARGMAX) {
-        unsigned long long best = 0;
-#pragma unroll 1
-        for (int c0 = 0; c0 < PBN; c0 += 16) {
-          float v[16];
-          tmem_ld16(trow + c0, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = n0 + c0 + i;
-            if (col < P.N) {
-              const unsigned long long key = argmax_key(r16(v[i]), col);
-              best = key > best ? key : best;
-            }
-          }
-        }
-        if (row < P.M) atomicMax(static_cast<unsigned long long*>(C) + row, best);
-      } else {
-        const bool vec = (P.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 &&
-                         (reinterpret_cast<uintptr_t>(R) & 15) == 0;
-        if (EPI == RWKV_EPI_RESID && vec && n0 + PBN <= P.N) {
-          // residual rows: fetch the thread's whole 128-column slice first, so the tile
-          // pays one memory latency per half instead of one per 16 columns
-#pragma unroll 1
-          for (int h0 = 0; h0 < PBN; h0 += 128) {
-            uint4 rr[16];
-            const __half* rp = R + (size_t)row * P.ldc + n0 + h0;
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              rr[i] = row < P.M ? *reinterpret_cast<const uint4*>(rp + 8 * i) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-            for (int c1 = 0; c1 < 128; c1 += 16) {
-              float v[16];
-              tmem_ld16(trow + h0 + c1, v);
-              if (row < P.M) {
-                uint4 pk[2];
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                  const __half2* r2 = reinterpret_cast<const __half2*>(&rr[c1 / 8 + q]);
-                  __half2* o2 = reinterpret_cast<__half2*>(&pk[q]);
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const float2 rf = __half22float2(r2[e]);
-                    o2[e] = __floats2half2_rn(rf.x + r16(v[8 * q + 2 * e]), rf.y + r16(v[8 * q + 2 * e + 1]));
-                  }
-                }
-                __half* cp = static_cast<__half*>(C) + (size_t)row * P.ldc + n0 + h0 + c1;
-                reinterpret_cast<uint4*>(cp)[0] = pk[0];
-                reinterpret_cast<uint4*>(cp)[1] = pk[1];
-              }
-            }
-          }
-        } else {
-#pragma unroll 1
-          for (int c0 = 0; c0 < PBN; c0 += 16) {
-            float v[16];
-            tmem_ld16(trow + c0, v);
-            const int col = n0 + c0;
-            if (row < P.M && col < P.N) store16<EPI>(v, C, R, row, col, P.N, P.ldc, vec, g);
-          }
-        }
-      }
+      persist_epilogue<EPI>(P, g, m0 + quad * 32 + lane, n0,
+                            tmem + (uint32_t)(b * PBN) + ((uint32_t)(quad * 32) << 16));
       // accumulator b is free again
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -722,6 +729,275 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * PBN));
   }
+}
+
+// ---------------------------------------------------------------------------
+// Two-SM variant of the persistent kernel (tcgen05 cta_group::2). A cluster of two
+// CTAs (a CTA pair on neighbouring SMs) owns 256 x 256 output tiles: each CTA TMA-loads
+// its own 128 rows of A and its own 128 rows (output columns) of B from this GPU's
+// memory -- no multicast -- so a pair moves 2 x 32 KB per K-block for an M=256 x N=256 x
+// K=64 product, against 48 KB per SM for the one-SM 128 x 256 tile. The even CTA (the
+// leader) issues tcgen05.mma.cta_group::2 (M = 256, N = 256) reading both CTAs' shared
+// memory; each CTA's TMEM receives its 128 rows of the accumulator, which its own four
+// epilogue warps drain. Synchronisation:
+//   full[s]   (leader)  both CTAs' copies complete_tx on it (mbarrier address with the
+//                       peer bit cleared); the leader's producer arms it for 64 KB
+//   empty[s]  (each)    the leader's commit multicast to both CTAs: stage s is free
+//   tfull[b]  (each)    the leader's commit multicast: accumulator b holds a tile
+//   tempty[b] (leader)  8 arrivals, the four epilogue warps of each CTA: b is drained
+constexpr int QBM = 256, QSTAGES = 6;
+constexpr uint32_t PEER_MASK = 0xFEFFFFFFu;  // shared::cluster address -> the even CTA's
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(saddr(bar) & PEER_MASK), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z),
+      "r"(z), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+// Arrive on barrier `bar` of both CTAs of the pair when the leader's MMAs so far complete.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(saddr(bar)), "h"((unsigned short)3)
+      : "memory");
+}
+// Arrive on the leader's copy of barrier `bar` (the same shared-memory offset).
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(saddr(bar)));
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_gemm_tc_pair(const __grid_constant__ TcParams prm, const __grid_constant__ TileMap tm) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int A_BYTES = BM * BK * 2, B_BYTES = (PBN / 2) * BK * 2;
+  unsigned char* sA = base;
+  unsigned char* sB = base + QSTAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + QSTAGES * B_BYTES);
+  uint64_t* empty = full + QSTAGES;
+  uint64_t* tfull = empty + QSTAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int total = tm.base[prm.n_problems];
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < QSTAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(tmem_slot)),
+                 "r"(2 * PBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers initialised before any remote arrival
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      int it = 0;
+      bool ok = true, waited = false;
+      for (int t = pair; t < total && ok; t += npairs) {
+        int g, m0, n0;
+        tile_of(prm, tm, t, g, m0, n0);
+        m0 = m0 * (QBM / BM);  // tile_of counts rows in BM units; pair tiles are QBM rows
+        const int am = m0 + (int)rank * BM, bn = n0 + (int)rank * (PBN / 2);
+        const int nk = (prm.p[g].K + BK - 1) / BK;
+        int pre = 0;
+        if (!waited) {  // the first tile's weight stages go out before the programmatic wait
+          pre = min(QSTAGES, nk);
+          for (int i = 0; i < pre; ++i) {
+            if (leader) mbar_expect_tx(&full[i], 2 * (A_BYTES + B_BYTES));
+            tma_load_2d_pair(sB + i * B_BYTES, &prm.tb[g], &full[i], i * BK, bn);
+          }
+          grid_dep_wait();
+          grid_dep_trigger();
+          waited = true;
+          for (int i = 0; i < pre; ++i)
+            tma_load_2d_pair(sA + i * A_BYTES, &prm.ta[g], &full[i], i * BK, am);
+          it = pre;
+        }
+        for (int kb = pre; kb < nk; ++kb, ++it) {
+          const int s = it % QSTAGES;
+          const uint32_t r = it / QSTAGES;
+          if (r > 0 && !mbar_wait(&empty[s], (r & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full[s], 2 * (A_BYTES + B_BYTES));
+          tma_load_2d_pair(sA + s * A_BYTES, &prm.ta[g], &full[s], kb * BK, am);
+          tma_load_2d_pair(sB + s * B_BYTES, &prm.tb[g], &full[s], kb * BK, bn);
+        }
+      }
+      if (!waited) {
+        grid_dep_wait();
+        grid_dep_trigger();
+      }
+      // drain: the last stages are free again once the leader's MMAs have read them
+      for (int i = max(0, it - QSTAGES); i < it; ++i) {
+        const uint32_t r = i / QSTAGES;
+        mbar_wait(&empty[i % QSTAGES], r & 1);
+      }
+    } else {
+      grid_dep_wait();
+      grid_dep_trigger();
+    }
+  } else if (warp == 1) {
+    grid_dep_wait();
+    grid_dep_trigger();
+    if (leader && lane == 0) {
+      // ---------------- MMA issuer (leader only) ----------------
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(PBN >> 3) << 17) | ((uint32_t)(QBM >> 4) << 24);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += npairs, ++j) {
+        int g, m0, n0;
+        tile_of(prm, tm, t, g, m0, n0);
+        const int nk = (prm.p[g].K + BK - 1) / BK;
+        const int b = j & 1;
+        const uint32_t u = (uint32_t)(j >> 1);
+        if (u > 0 && !mbar_wait(&tempty[b], (u & 1) ^ 1)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + (uint32_t)(b * PBN);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % QSTAGES;
+          if (!mbar_wait(&full[s], (it / QSTAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t ad = smem_desc_sw128(sA + s * A_BYTES);
+          const uint64_t bd = smem_desc_sw128(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16_pair(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), idesc,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(&empty[s]);
+        }
+        if (ok) umma_commit_pair(&tfull[b]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    grid_dep_wait();
+    grid_dep_trigger();
+    const int quad = warp & 3;
+    int j = 0;
+    for (int t = pair; t < total; t += npairs, ++j) {
+      const int b = j & 1;
+      const bool ok = mbar_wait(&tfull[b], (uint32_t)(j >> 1) & 1);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (!__all_sync(0xffffffffu, ok)) break;
+      int g, m0, n0;
+      tile_of(prm, tm, t, g, m0, n0);
+      m0 = m0 * (QBM / BM) + (int)rank * BM;
+      persist_epilogue<EPI>(prm.p[g], g, m0 + quad * 32 + lane, n0,
+                            tmem + (uint32_t)(b * PBN) + ((uint32_t)(quad * 32) << 16));
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_leader(&tempty[b]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the pair's MMAs may still use its memory
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * PBN));
+  }
+}
+
+constexpr int pair_smem_bytes() {
+  return 1024 + QSTAGES * (BM * BK * 2 + (PBN / 2) * BK * 2) + (2 * QSTAGES + 4) * 8 + 16;
+}
+
+// Launch of the pair kernel: clusters of two CTAs, as many pairs as can be resident
+// (cudaOccupancyMaxActiveClusters), each walking 256 x 256 tiles.
+template <int EPI>
+int launch_tc_pair(const TcParams& prm, const TileMap& tm, cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool done[64] = {};
+  static int max_clusters[64] = {};
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = pair_smem_bytes();
+  cfg.stream = st;
+  cfg.attrs = attr;
+  if (dev < 64 && !done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc_pair<EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pair_smem_bytes());
+    int n = 0;
+    if (e == cudaSuccess) {
+      cfg.gridDim = dim3(148);
+      cfg.numAttrs = 1;
+      e = cudaOccupancyMaxActiveClusters(&n, k_gemm_tc_pair<EPI>, &cfg);
+    }
+    if (e != cudaSuccess || n < 1) {
+      rwkv_set_error("gemm_tc_pair: setup: %s (%d clusters)", cudaGetErrorString(e), n);
+      return RWKV_ERR_CUDA;
+    }
+    max_clusters[dev] = n;
+    done[dev] = true;
+  }
+  const int total = tm.base[prm.n_problems];
+  const int pairs = min(total, dev < 64 ? max_clusters[dev] : 70);
+  cfg.gridDim = dim3(2 * pairs);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = rwkv_chain_take_pdl() ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc_pair<EPI>, prm, tm);
+  if (e != cudaSuccess) {
+    rwkv_set_error("gemm_tc_pair: launch failed: %s", cudaGetErrorString(e));
+    return RWKV_ERR_CUDA;
+  }
+  return rwkv_check_launch("gemm_tc_pair");
 }
 
 constexpr int persist_smem_bytes() {
@@ -767,8 +1043,39 @@ bool gemm_persist_enabled() {
   return on;
 }
 
-// Persistent 128 x 256 tiles over every problem of the group (splits = 1).
+// SM count of the current device (cached per device).
+static int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// RWKV_B200_GEMM_PAIR=0 keeps large problems on the one-SM persistent kernel.
+bool gemm_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("RWKV_B200_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Persistent tiles over every problem of the group (splits = 1): 256 x 256 on CTA pairs
+// (cta_group::2), or 128 x 256 on single CTAs.
 int gemm_tc_launch_persist(const rwkv7_gemm_problem* p, int n, int epi, cudaStream_t st) {
+  // CTA pairs when they all get a tile (>= one 256 x 256 tile per pair); a group of fewer
+  // tiles (e.g. the prefill FFN value, 64 tiles) runs faster on the single-CTA kernel,
+  // whose 128-row tiles reach more SMs
+  int pair_tiles = 0;
+  for (int i = 0; i < n; ++i) pair_tiles += ((p[i].M + QBM - 1) / QBM) * ((p[i].N + PBN - 1) / PBN);
+  const bool pair = gemm_pair_enabled() && pair_tiles >= device_sm_count() / 2;
+  const int tile_m = pair ? QBM : BM, box_n = pair ? PBN / 2 : PBN;
   TcParams prm;
   TileMap tm;
   memset(&prm, 0, sizeof(prm));
@@ -778,7 +1085,7 @@ int gemm_tc_launch_persist(const rwkv7_gemm_problem* p, int n, int epi, cudaStre
   for (int i = 0; i < n; ++i) {
     int rc = make_map(&prm.ta[i], p[i].A, p[i].M, p[i].K, p[i].lda, BM);
     if (rc) return rc;
-    rc = make_map(&prm.tb[i], p[i].B, p[i].N, p[i].K, p[i].ldb, PBN);
+    rc = make_map(&prm.tb[i], p[i].B, p[i].N, p[i].K, p[i].ldb, box_n);
     if (rc) return rc;
     prm.p[i].C = p[i].C;
     prm.p[i].R = p[i].R;
@@ -786,8 +1093,15 @@ int gemm_tc_launch_persist(const rwkv7_gemm_problem* p, int n, int epi, cudaStre
     prm.p[i].N = p[i].N;
     prm.p[i].K = p[i].K;
     prm.p[i].ldc = p[i].ldc;
-    tm.tiles_m[i] = (p[i].M + BM - 1) / BM;
+    tm.tiles_m[i] = (p[i].M + tile_m - 1) / tile_m;
     tm.base[i + 1] = tm.base[i] + tm.tiles_m[i] * ((p[i].N + PBN - 1) / PBN);
+  }
+  if (pair) switch (epi) {
+    case RWKV_EPI_STORE: return launch_tc_pair<RWKV_EPI_STORE>(prm, tm, st);
+    case RWKV_EPI_RESID: return launch_tc_pair<RWKV_EPI_RESID>(prm, tm, st);
+    case RWKV_EPI_RELUSQ: return launch_tc_pair<RWKV_EPI_RELUSQ>(prm, tm, st);
+    case RWKV_EPI_STORE_F32: return launch_tc_pair<RWKV_EPI_STORE_F32>(prm, tm, st);
+    case EPI_ARGMAX: return launch_tc_pair<EPI_ARGMAX>(prm, tm, st);
   }
   switch (epi) {
     case RWKV_EPI_STORE: return launch_tc_persist<RWKV_EPI_STORE>(prm, tm, st);
@@ -808,19 +1122,6 @@ int gemm_tc_launch_persist(const rwkv7_gemm_problem* p, int n, int epi, cudaStre
 // non-null the split-K reduce is left to the consumer: *splits_out receives the
 // number of K-slices parked in ws ([splits][M][N] fp32 per problem, problems back to
 // back), 1 when the GEMM wrote its output directly.
-// SM count of the current device (cached per device).
-static int device_sm_count() {
-  static int cache[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!cache[dev]) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
-  }
-  return cache[dev];
-}
 
 int gemm_tc_launch(const rwkv7_gemm_problem* p, int n, int epi, float* ws, size_t ws_floats,
                    cudaStream_t st, int* splits_out) {
