@@ -49,6 +49,11 @@ constexpr int RSA = KD, RSB = KD + 4;
 #define SEG_CHUNKS 8  // measured at T=4096: 8 beats 16 (0.5 %) and 32 (-5 %)
 #endif
 constexpr int SEG = SEG_CHUNKS;
+// chunks of a segment corrected by one k_seg_fix CTA (a divisor of SEG)
+#ifndef FIX_CHUNKS
+#define FIX_CHUNKS 4  // measured at T=4096: 4 beats 8 (one CTA per segment) by 0.5 %, 2 and 1
+#endif
+static_assert(SEG % FIX_CHUNKS == 0, "FIX_CHUNKS must divide SEG_CHUNKS");
 }  // namespace
 
 // chunk_cu[s] = chunks before sequence s, seg_cu[s] = segments (SEG chunks each) before
@@ -815,12 +820,18 @@ __global__ void __launch_bounds__(256) k_seg_fix(const int* __restrict__ cu,
   RWKV_GRID_DEP_ENTRY();
   __shared__ __align__(16) float Ss[KD * WQ_LD];
   __shared__ __align__(16) float Qs[CL * WQ_LD];
-  const int gs = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
+  // blockIdx.x = segment * (SEG / FIX_CHUNKS) + part: each CTA corrects FIX_CHUNKS
+  // chunks of one segment, so the chunks of a segment are corrected in parallel
+  const int gs = blockIdx.x / (SEG / FIX_CHUNKS), part = blockIdx.x % (SEG / FIX_CHUNKS);
+  const int h = blockIdx.y, H = gridDim.y, tid = threadIdx.x;
   if (gs >= seg_cu[S]) return;
   const int s = seq_of(seg_cu, S, gs);
   const int nseg = seg_cu[s + 1] - seg_cu[s], g = gs - seg_cu[s];
   if (nseg < 2 || g == 0) return;
-  const int c0 = chunk_cu[s] + g * SEG, c1 = min(chunk_cu[s + 1], c0 + SEG);
+  const int cseg = chunk_cu[s] + g * SEG;
+  const int c0 = cseg + part * FIX_CHUNKS;
+  const int c1 = min(min(chunk_cu[s + 1], cseg + SEG), c0 + FIX_CHUNKS);
+  if (c0 >= c1) return;
   const size_t so = ((size_t)gs * H + h) * KD * KD;
   for (int i = tid; i < KD * KD / 4; i += 256) {
     const int r = i / (KD / 4), cc = (i % (KD / 4)) * 4;
@@ -1048,7 +1059,8 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   if ((rc = rwkv_launch("seg_combine", k_seg_combine, dim3(S, H, 4), dim3(256), 0, st, cs.seg_cu,
                         slots, cs.lbuf, cs.phi, cs.sst, rnn)))
     return rc;
-  return rwkv_launch("seg_fix", k_seg_fix, dim3(maxs, H), dim3(256), 0, st, cu, chunk_cu,
+  return rwkv_launch("seg_fix", k_seg_fix, dim3(maxs * (SEG / FIX_CHUNKS), H), dim3(256), 0, st,
+                     cu, chunk_cu,
                      cs.seg_cu, S, cs.qt, cs.sst, cs.yf32, ybuf, C);
 }
 
