@@ -161,6 +161,14 @@ template <int EPI>
 __device__ __forceinline__ void store16(const float (&v)[16], void* Cv, const __half* R, int row,
                                         int col, int N, int ldc, bool vec, int prob) {
   const size_t o = (size_t)row * ldc + col;
+  if (EPI == RWKV_EPI_STORE_F32 && col + 16 <= N && (ldc & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(Cv) & 15) == 0) {
+    // four 16-byte stores: the epilogue's cost is per store instruction
+    float4* C = reinterpret_cast<float4*>(static_cast<float*>(Cv) + o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) C[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    return;
+  }
   if (EPI != RWKV_EPI_STORE_F32 && EPI != RWKV_EPI_LORA_ACT2 && col + 16 <= N && vec) {
     __half* C = static_cast<__half*>(Cv);
     uint4 pk[2];
