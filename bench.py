@@ -371,20 +371,25 @@ def wkv_kernel_roofline(lib, B: int, H: int, dev, stream, peak: float) -> dict:
     vec = [torch.randn(B, C, generator=g, device=dev).half() for _ in range(7)]
     cst = [torch.randn(C, generator=g, device=dev).half() for _ in range(3)]
     out = torch.empty(B, C, dtype=torch.float16, device=dev)
-    h = stream.cuda_stream
-
-    it = [0]
-
-    def launch():
-        S = states[it[0] % len(states)]
-        it[0] += 1
+    def launch(S, h):
         _lib.check(lib.rwkv7_wkv_gn_step(S.data_ptr(), None, *[t.data_ptr() for t in vec],
                                          *[t.data_ptr() for t in cst], out.data_ptr(), B, H, 0, h))
 
-    for _ in range(5):
-        launch()
-    n = 240  # ten passes over the 24 state blocks
-    ms = timed(launch, n, stream)
+    for i in range(5):
+        launch(states[i], stream.cuda_stream)
+    # the 24 launches (one per state block) captured in a CUDA graph, so that the timed
+    # replays measure the kernel back to back rather than the host's launch rate
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap):
+        for S in states:
+            launch(S, cap.cuda_stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):  # replays go to the stream the events are recorded on
+        graph.replay()
+        n = 10  # ten passes over the 24 state blocks
+        ms = timed(graph.replay, n, stream) / len(states)
     # per launch: fp32 state read + write, 7 fp16 input vectors, 1 fp16 output vector
     algo = B * H * 64 * 64 * 4 * 2 + 8 * B * C * 2
     achieved = algo / (ms * 1e-3) / 1e9
