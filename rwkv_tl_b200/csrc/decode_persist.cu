@@ -673,18 +673,8 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
         return __half22float2(*reinterpret_cast<const __half2*>(sBc + v * 64 + 2 * lane));
       };
       const float2 RK = bvec(5), LW = bvec(6), LB = bvec(7);
-      // activated ranks (gates.py:166-181: tanh for w, sigmoid for g, fp32), split into
-      // fp16 hi + lo so that the tensor cores see them to ~22 bits
-      for (int i = tid; i < NB * RWKV_RANK_SUM; i += NT) {
-        const int b = i / RWKV_RANK_SUM, j = i % RWKV_RANK_SUM;
-        float v = b < B ? ldcg_h(P.ranks + (size_t)b * RWKV_RANK_SUM + j) : 0.f;
-        if (j >= 32 && j < 96) v = tanhf(v);
-        else if (j >= 160) v = sigmoidf_(v);
-        const __half hi = f2h(v);
-        srh[b * SLD + j] = hi;
-        srl[b * SLD + j] = f2h(v - h2f(hi));
-      }
-      // gate inputs: thread (sequence gb, channel gc) of this head
+      // gate inputs: thread (sequence gb, channel gc) of this head; all of this phase's
+      // L2 reads are issued before any of them is used
       const int gb = tid >> 6, gc = tid & 63;
       float r_in = 0.f, k_in = 0.f, v_in = 0.f, vf_in = 0.f;
       if (gb < B) {
@@ -693,6 +683,36 @@ __global__ void __launch_bounds__(NT, 1) k_dec_persist(const __grid_constant__ P
         k_in = ldcg_h(P.rkv + BC + o);
         v_in = ldcg_h(P.rkv + 2 * BC + o);
         if (l > 0) vf_in = ldcg_h(P.vfirst + o);
+      }
+      // activated ranks (gates.py:166-181: tanh for w, sigmoid for g, fp32), split into
+      // fp16 hi + lo so that the tensor cores see them to ~22 bits. One or two sequences:
+      // every rank load issued before the first is used (measured: B = 1 and 2 gain, the
+      // four-sequence layout loses)
+      auto act_store = [&](int i, float v) {
+        const int b = i / RWKV_RANK_SUM, j = i % RWKV_RANK_SUM;
+        if (j >= 32 && j < 96) v = tanhf(v);
+        else if (j >= 160) v = sigmoidf_(v);
+        const __half hi = f2h(v);
+        srh[b * SLD + j] = hi;
+        srl[b * SLD + j] = f2h(v - h2f(hi));
+      };
+      auto ld_rank = [&](int i) {
+        const int b = i / RWKV_RANK_SUM, j = i % RWKV_RANK_SUM;
+        return b < B ? ldcg_h(P.ranks + (size_t)b * RWKV_RANK_SUM + j) : 0.f;
+      };
+      if constexpr (NB <= 2) {
+        constexpr int RIT = (NB * RWKV_RANK_SUM + NT - 1) / NT;
+        float rv[RIT];
+#pragma unroll
+        for (int u = 0; u < RIT; ++u) {
+          const int i = tid + u * NT;
+          rv[u] = i < NB * RWKV_RANK_SUM ? ld_rank(i) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < RIT; ++u)
+          if (tid + u * NT < NB * RWKV_RANK_SUM) act_store(tid + u * NT, rv[u]);
+      } else {
+        for (int i = tid; i < NB * RWKV_RANK_SUM; i += NT) act_store(i, ld_rank(i));
       }
       __syncthreads();
       if (l == 10) STAMP(146);
