@@ -174,6 +174,36 @@ class CUDAGraph(RWKV7Model):
             return logits
         return e.logits.clone()
 
+    def decode_batch_greedy(self, tokens: Tensor, state: BatchedState,
+                            slots: Tensor | None = None, out: Tensor | None = None) -> Tensor:
+        """Graph-replayed ``decode_batch_greedy``: one decode step, greedy next ids ``[B]``.
+
+        A caller-provided ``out`` is captured as the graph's output (keyed by its
+        address); without one the graph owns its id buffer and the caller gets a copy.
+        """
+        tok = self.model._tokens(tokens)
+        B = tok.numel()
+        key = ("decg", B, state.rnn.data_ptr(), None if slots is None else slots.data_ptr(),
+               None if out is None else out.data_ptr())
+        e = self._get(key)
+        if e is None and key not in self._failed:
+            buf = torch.zeros(B, dtype=torch.long, device=self.w.device)
+            ids = out if out is not None else torch.empty(B, dtype=torch.long,
+                                                          device=self.w.device)
+            scratch = BatchedState(self.L, self.C, state.n_slots, device=self.w.device)
+            g = self._capture(key, lambda st: self.model.decode_batch_greedy(buf, st, slots, ids),
+                              scratch, state, f"decode_batch_greedy(B={B})")
+            if g is not None:
+                e = _Entry(g, buf, ids)
+                self._put(key, e)
+        if e is None:
+            return self.model.decode_batch_greedy(tok, state, slots, out)
+        e.tok.copy_(tok, non_blocking=True)
+        e.graph.replay()
+        if out is not None:
+            return out
+        return e.logits.clone()
+
     def prefill_batch(self, seqs, state, slots=None):
         return self.model.prefill_batch(seqs, state, slots)
 

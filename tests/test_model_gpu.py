@@ -168,6 +168,30 @@ def test_graph_wrapper_matches_eager():
         assert torch.equal(x["rnn"], y["rnn"])
 
 
+@pytest.mark.parametrize("B", [2, 64])
+def test_graph_greedy_matches_eager_greedy(B):
+    """The graph wrapper's decode_batch_greedy replays the eager greedy step exactly:
+    same ids every step (with and without a caller-provided id buffer) and same states."""
+    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 5)
+    gm = make_rwkv7(torch.device("cuda"), backend="b200")(m.w)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    states = [BatchedState(m.L, m.C, B, device="cuda") for _ in range(2)]
+    for t in ("rnn", "tmix_x", "cmix_x"):
+        src = torch.randn(getattr(states[0], t).shape, generator=g, device="cuda")
+        src = 0.1 * src if t == "rnn" else src.half()
+        for bs in states:
+            getattr(bs, t).copy_(src)
+    toks = torch.randint(0, 4096, (B,), generator=g, device="cuda")
+    out = torch.empty(B, dtype=torch.int64, device="cuda")
+    a_ids, b_ids = toks.clone(), toks.clone()
+    for step in range(4):
+        a_ids = m.decode_batch_greedy(a_ids, states[0])
+        b_ids = gm.decode_batch_greedy(b_ids, states[1], out=out if step % 2 else None).clone()
+        assert torch.equal(a_ids, b_ids), step
+    for t in ("rnn", "tmix_x", "cmix_x"):
+        assert torch.equal(getattr(states[0], t), getattr(states[1], t))
+
+
 def test_graph_replay_after_workspace_growth():
     """A captured graph keeps working after later calls grew the model's scratch.
 
