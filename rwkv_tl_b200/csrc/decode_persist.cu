@@ -65,7 +65,7 @@ constexpr int PMAXL = 24;
 constexpr int MAXG = 160;  // CTAs (SMs) at most
 constexpr int RA = 24;     // phase-A rows per task (multiple of 8)
 constexpr int FROWS = 32;  // FFN hidden rows per CTA at most (groups of 8)
-constexpr int NREP = 4;    // replicas of the FFN accumulator (CTA c adds into c % NREP)
+constexpr int NREP = 2;    // replicas of the FFN accumulator (CTA c adds into c % NREP; measured: 2 beats 1 and 4)
 constexpr uint64_t WAIT_NS = 200000000ull;
 
 struct GridBar {
