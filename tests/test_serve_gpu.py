@@ -9,6 +9,7 @@ import torch
 
 from rwkv_tl_b200 import ContinuousBatcher, Request, RWKV7Weight, State, make_rwkv7
 from rwkv_tl_b200.synth import ModelConfig, synth_checkpoint
+from tests._util import ARGMAX_GAP, OraclePair
 
 pytestmark = pytest.mark.gpu
 
@@ -43,3 +44,36 @@ def test_continuous_batching_matches_sequential_generate():
     from rwkv_tl_b200 import _lib
 
     assert _lib.load().rwkv_b200_device_error() == 0
+
+
+def test_continuous_batching_matches_the_oracle():
+    """The batcher's greedy tokens against the fp64 oracle of the reference's rounding
+    schedules (prompt but its last token through prefill, the rest through decode), teacher-
+    forced: wherever the oracle's top-2 gap is clear (the reference benchmark's rule), the
+    batcher picked the oracle's argmax."""
+    cfg = ModelConfig(n_layer=2, n_embd=768, vocab=4096)
+    dev = torch.device("cuda")
+    sd = synth_checkpoint(cfg, seed=6)
+    w = RWKV7Weight(sd, device=dev)
+    o = OraclePair(sd)
+    m = make_rwkv7(dev, backend="b200", use_graph=False)(w)
+    g = torch.Generator().manual_seed(8)
+    lens = [1, 4, 23, 61, 2, 90]
+    reqs = [Request(i, torch.randint(0, cfg.vocab, (L,), generator=g), 4 + i % 3)
+            for i, L in enumerate(lens)]
+    b = ContinuousBatcher(m, max_batch=3, prefill_tokens=40)
+    for r in reqs:
+        b.submit(r)
+    b.run()
+    checked = 0
+    for r in reqs:
+        assert len(r.output) == r.max_new_tokens
+        So = o.state()
+        ref = o.forward(r.prompt.tolist(), So)[0]
+        for t in r.output:
+            top2 = torch.topk(ref.double().cpu(), 2).values
+            if float(top2[0] - top2[1]) > ARGMAX_GAP:
+                assert t == int(ref.argmax()), (r.rid, t, int(ref.argmax()))
+                checked += 1
+            ref = o.decode(t, So)[0]
+    assert checked >= 10
