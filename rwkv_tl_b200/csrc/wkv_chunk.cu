@@ -18,6 +18,7 @@
 // with the fp32 state of 8 rows in registers (one warp per row). All math is
 // fp32; exponents stay within one chunk (|G| <= 16 * 0.6066), so no overflow.
 #include <climits>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -26,7 +27,10 @@ namespace {
 __device__ int g_chunk_bad = 0;  // 1: a sequence / chunk table out of range; 2: a scan wait gave up
 constexpr int CL = 16;                       // chunk length
 constexpr int KD = RWKV_HD;                  // 64
-constexpr int RWS = 2 * CL + KD;             // per-row floats: PU v | PY v | U
+#ifndef RWS_PAD
+#define RWS_PAD 4  // 400-byte rows: consecutive rows' 16-byte loads fall on distinct banks
+#endif
+constexpr int RWS = 2 * CL + KD + RWS_PAD;   // per-row floats: PU v | PY v | U | pad
 constexpr int SHARED_F = 3 * CL * KD + KD;    // row-independent part of a record
 constexpr int REC = SHARED_F + KD * RWS;      // floats per (chunk, head) record
 // record layout (floats): What[CL][KD] | Q[CL][KD] | Bt[CL][KD] | gL[KD] |
@@ -742,6 +746,373 @@ __global__ void __launch_bounds__(SCAN_THREADS, SCAN_MINB) k_scan_phi(
                   yf32, lbuf, S, C, M, max_chunks, n_slots);
 }
 
+// ---- segment scan on the tensor cores (tcgen05, kind::tf32) --------------------------
+//
+// One CTA per (segment, head), 256 threads; thread (row, half): row = TMEM lane (its
+// warp's lane quadrant), half = keys 32 half .. + 31 of that row of a 128 x 64 fp32 state
+// block. Rows 0..63 are the head's state rows (the true state for a sequence's first
+// segment, zero for the others); rows 64..127 basis rows e_j (later segments only), which
+// carry no value terms. Per chunk, the 16 + 16 dot products of every row with What and Q
+// are ONE tcgen05.mma chain, M = 128, N = 32, K = 64: the state block is the A operand in
+// TMEM (written by its threads with tcgen05.st), [What; Q] the B operand in shared memory;
+// every fp32 operand is split into tf32 hi + lo and D = A_lo B_hi + A_hi B_lo + A_hi B_hi
+// accumulates in fp32 (about fp32 accuracy). A row's D gives its in-chunk states
+// sa = What s + PU v and outputs y = Q s + PY v; the state then advances on the CUDA
+// cores, s <- s * gL + U + sum_t sa_t Bt_t. For a basis row j the outputs are column j of
+// Q_c Phi_c (qt, for k_seg_fix) and its final state column j of the segment's transfer
+// matrix (phi, for k_seg_combine): the transfer matrices come out of the same MMAs. Each
+// chunk record (row-independent part and every row's value terms) arrives by one bulk
+// copy into a two-stage ring.
+namespace {
+constexpr int TS_ROWS = 128;
+constexpr int TS_THREADS = 256;
+constexpr uint32_t TS_TMEM_COLS = 256;  // A hi [0, 64), A lo [64, 128), D [128, 160)
+constexpr uint32_t TS_B_BLK = 2 * CL * 128;       // 4 KiB: a 32-wide K-block of [What; Q]
+constexpr uint32_t TS_OFF_BHI = 0, TS_OFF_BLO = 2 * TS_B_BLK;
+constexpr uint32_t TS_OFF_REC = 4 * TS_B_BLK;
+constexpr uint32_t TS_REC_BYTES = REC * 4;
+constexpr uint32_t TS_OFF_BAR = TS_OFF_REC + 2 * TS_REC_BYTES;
+}  // namespace
+constexpr size_t TS_SMEM = 1024 + TS_OFF_BAR + 64;
+
+// byte offset of element (row r, column kk < 32) in a 128-byte swizzled K-major block
+__device__ __forceinline__ uint32_t ts_sw(int r, int kk) {
+  return (uint32_t)(((r >> 3) << 10) + ((r & 7) << 7) + ((((kk >> 2) ^ (r & 7))) << 4) + ((kk & 3) << 2));
+}
+__device__ __forceinline__ uint64_t ts_desc(uint32_t saddr_tile) {
+  uint64_t d = (uint64_t)((saddr_tile >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;            // 128-byte swizzle
+  return d;
+}
+__device__ __forceinline__ void ts_st4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t ts_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+// 16 consecutive 32-bit TMEM columns of this thread's lane <- v
+__device__ __forceinline__ void ts_tst16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void ts_tld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15},"
+      " [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(TS_THREADS, 2) k_seg_scan_tc(
+    const float* __restrict__ rec, const int* __restrict__ cu, const int* __restrict__ chunk_cu,
+    const int* __restrict__ seg_cu, const int* __restrict__ slots, float* __restrict__ rnn,
+    __half* __restrict__ ybuf, float* __restrict__ yf32, float* __restrict__ lbuf,
+    float* __restrict__ qt, float* __restrict__ phi, int S, int H, int C, int M, int max_chunks,
+    int n_slots) {
+  RWKV_GRID_DEP_ENTRY();
+  extern __shared__ unsigned char ts_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(ts_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = sm_addr(base);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + TS_OFF_BAR);  // [2] record stages
+  uint64_t* mma_bar = full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int gs = blockIdx.x / H, h = blockIdx.x % H;
+  if (gs >= seg_cu[S]) return;
+  const int s = seq_of(seg_cu, S, gs);
+  const int slot = slots ? slots[s] : s;
+  const int cs = chunk_cu[s], ce = chunk_cu[s + 1];
+  const int nseg = seg_cu[s + 1] - seg_cu[s], g = gs - seg_cu[s];
+  const int m_seq = cu[s], m_end = cu[s + 1];
+  if (slot < 0 || slot >= n_slots || cs < 0 || ce < cs || ce > max_chunks || m_seq < 0 ||
+      m_end < m_seq || m_end > M || (m_end - m_seq + CL - 1) / CL != ce - cs ||
+      nseg != (ce - cs + SEG - 1) / SEG) {
+    if (tid == 0) atomicOr(&g_chunk_bad, 1);
+    return;
+  }
+  const int c0 = cs + g * SEG, c1 = min(ce, c0 + SEG);
+  const int m_beg = m_seq + g * SEG * CL;
+  const int row = tid & (TS_ROWS - 1), half = tid >> 7, k0 = 32 * half;
+  const bool basis = row >= KD, need_basis = g > 0;  // basis rows matter for later segments
+  const int vrow = row & (KD - 1);
+
+  if (tid == 0) {
+    sc_mbar_init(&full[0], 1);
+    sc_mbar_init(&full[1], 1);
+    sc_mbar_init(mma_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     sm_addr(tmem_slot)), "r"(TS_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+
+  int issued = 0, waited = 0;  // record copies issued (thread 0) / waited for
+  auto issue = [&](int c) {
+    const int buf = (c - c0) & 1;
+    sc_mbar_expect_tx(&full[buf], TS_REC_BYTES);
+    sc_bulk_g2s(base + TS_OFF_REC + buf * TS_REC_BYTES, rec + ((size_t)c * H + h) * REC,
+                TS_REC_BYTES, &full[buf]);
+    ++issued;
+  };
+  if (tid == 0) issue(c0);
+
+  // this thread's half row of the state block
+  float st[32];
+  if (!basis && g == 0) {
+    const float4* S0 =
+        reinterpret_cast<const float4*>(rnn + (((size_t)slot * H + h) * KD + vrow) * KD + k0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 v = S0[q];
+      st[4 * q] = v.x; st[4 * q + 1] = v.y; st[4 * q + 2] = v.z; st[4 * q + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) st[k] = (basis && need_basis && k0 + k == vrow) ? 1.f : 0.f;
+  }
+
+  const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(2 * CL >> 3) << 17) |
+                         ((uint32_t)(TS_ROWS >> 4) << 24);   // N = 32: [What; Q]
+  const uint32_t idesc2 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(KD >> 3) << 17) |
+                          ((uint32_t)(TS_ROWS >> 4) << 24);  // N = 64: Bt^T
+  bool ok = true;
+  for (int c = c0; c < c1; ++c) {
+    const int it = c - c0, buf = it & 1;
+    // the other stage is free (its chunk's readers passed the last barrier): next record
+    if (tid == 0 && c + 1 < c1) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(c + 1);
+    }
+    // A: this half row as tf32 hi / lo into TMEM columns [k0, k0 + 32) and [64 + k0, ..)
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float x = st[16 * p + e];
+        hi[e] = ts_tf32(x);
+        lo[e] = __float_as_uint(x - __uint_as_float(hi[e]));  // the MMA reads its top 19 bits
+      }
+      ts_tst16(lane_base + (uint32_t)(k0 + 16 * p), hi);
+      ts_tst16(lane_base + (uint32_t)(64 + k0 + 16 * p), lo);
+    }
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    // B: [What; Q] of the chunk (32 rows x 64) as tf32 hi / lo, from the record stage
+    ok = ok && sc_mbar_wait(&full[buf], (it >> 1) & 1);
+    waited += ok ? 1 : 0;
+    const float* R = reinterpret_cast<const float*>(base + TS_OFF_REC + buf * TS_REC_BYTES);
+    {
+      const int n = tid >> 3, kb0 = (tid & 7) * 8;  // 32 rows x 8 pieces of 8
+      const float* src = R + (n < CL ? OFF_W + n * KD : OFF_Q + (n - CL) * KD) + kb0;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float4 v = reinterpret_cast<const float4*>(src)[q];
+        const float xs[4] = {v.x, v.y, v.z, v.w};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          hi[e] = ts_tf32(xs[e]);
+          lo[e] = ts_tf32(xs[e] - __uint_as_float(hi[e]));
+        }
+        const int kk = kb0 + 4 * q;
+        const uint32_t o = (kk >> 5) * TS_B_BLK + ts_sw(n, kk & 31);
+        ts_st4(sb + TS_OFF_BHI + o, hi[0], hi[1], hi[2], hi[3]);
+        ts_st4(sb + TS_OFF_BLO + o, lo[0], lo[1], lo[2], lo[3]);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      // D = A_lo B_hi + A_hi B_lo + A_hi B_hi over K = 64 (8 steps of K = 8 per pass)
+#pragma unroll
+      for (int pass = 0; pass < 3; ++pass)
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+          const uint32_t acol = (pass == 0 ? 64u : 0u) + 32u * kb;
+          const uint64_t bd = ts_desc(sb + (pass == 1 ? TS_OFF_BLO : TS_OFF_BHI) + kb * TS_B_BLK);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t accum = (pass | kb | ks) ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem + 128u),
+                "r"(tmem + acol + 8u * ks), "l"(bd + (uint64_t)(2 * ks)), "r"(idesc), "r"(accum));
+          }
+        }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       sm_addr(mma_bar))
+                   : "memory");
+    }
+    ok = __syncthreads_and(sc_mbar_wait(mma_bar, 0)) != 0;
+    if (!ok) break;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // D row: columns 0..15 What s, 16..31 Q s
+    float sa[CL], dq[CL];
+    ts_tld16(lane_base + 128u, sa);
+    ts_tld16(lane_base + 128u + CL, dq);
+    const float* RW = R + OFF_RW + vrow * RWS;  // this state row's value terms
+    if (!basis) {
+#pragma unroll
+      for (int q = 0; q < CL / 4; ++q) {
+        const float4 a = reinterpret_cast<const float4*>(RW)[q];
+        sa[4 * q] += a.x; sa[4 * q + 1] += a.y; sa[4 * q + 2] += a.z; sa[4 * q + 3] += a.w;
+      }
+    }
+    // the second product, sum_t sa_t Bt_t (M = 128, N = 64, K = 16): sa as tf32 hi / lo into
+    // TMEM columns [0, 16) / [64, 80) (the first half of each row), Bt^T into the B tiles
+    if (half == 0) {
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        hi[e] = ts_tf32(sa[e]);
+        lo[e] = __float_as_uint(sa[e] - __uint_as_float(hi[e]));
+      }
+      ts_tst16(lane_base, hi);
+      ts_tst16(lane_base + 64u, lo);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    {
+      const int n = tid >> 2, t0 = (tid & 3) * 4;  // 64 rows n (keys) x 4 groups of 4 t
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float x = R[OFF_B + (t0 + e) * KD + n];
+        hi[e] = ts_tf32(x);
+        lo[e] = __float_as_uint(x - __uint_as_float(hi[e]));
+      }
+      const uint32_t o = ts_sw(n, t0);
+      ts_st4(sb + TS_OFF_BHI + o, hi[0], hi[1], hi[2], hi[3]);
+      ts_st4(sb + TS_OFF_BLO + o, lo[0], lo[1], lo[2], lo[3]);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int pass = 0; pass < 3; ++pass) {
+        const uint32_t acol = pass == 0 ? 64u : 0u;
+        const uint64_t bd = ts_desc(sb + (pass == 1 ? TS_OFF_BLO : TS_OFF_BHI));
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint32_t accum = (pass | ks) ? 1u : 0u;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\t"
+              "setp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem + 160u),
+              "r"(tmem + acol + 8u * ks), "l"(bd + (uint64_t)(2 * ks)), "r"(idesc2), "r"(accum));
+        }
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       sm_addr(mma_bar))
+                   : "memory");
+    }
+    // outputs while the second product runs (the first half of each row writes them)
+    const int mc = m_beg + it * CL;  // first token of the chunk
+    if (!basis) {
+      if (half == 0) {
+        const int nt = min(CL, m_end - mc);
+        float y[CL];
+#pragma unroll
+        for (int q = 0; q < CL / 4; ++q) {
+          const float4 b = reinterpret_cast<const float4*>(RW + CL)[q];
+          y[4 * q] = dq[4 * q] + b.x; y[4 * q + 1] = dq[4 * q + 1] + b.y;
+          y[4 * q + 2] = dq[4 * q + 2] + b.z; y[4 * q + 3] = dq[4 * q + 3] + b.w;
+        }
+        if (g == 0) {
+          __half* yp = ybuf + (size_t)mc * C + h * KD + vrow;  // final outputs
+#pragma unroll
+          for (int t = 0; t < CL; ++t) {
+            if (t < nt) *yp = f2h(y[t]);
+            yp += C;
+          }
+        } else {
+          float* yp = yf32 + (size_t)mc * C + h * KD + vrow;  // partial: k_seg_fix adds
+#pragma unroll                                                // the incoming state's part
+          for (int t = 0; t < CL; ++t) {
+            if (t < nt) *yp = y[t];
+            yp += C;
+          }
+        }
+      }
+    } else if (need_basis && half == 0) {
+      float* q = qt + ((size_t)c * H + h) * (CL * KD) + vrow;
+#pragma unroll
+      for (int t = 0; t < CL; ++t) q[t * KD] = dq[t];
+    }
+    // s <- s * gL + U + sum_t sa_t Bt_t over this thread's keys
+    ok = __syncthreads_and(sc_mbar_wait(mma_bar, 1)) != 0;
+    if (!ok) break;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    {
+      float d2[32];
+      ts_tld16(lane_base + 160u + k0, *reinterpret_cast<float(*)[16]>(d2));
+      ts_tld16(lane_base + 160u + k0 + 16, *reinterpret_cast<float(*)[16]>(d2 + 16));
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      const float4* gl4 = reinterpret_cast<const float4*>(R + OFF_G + k0);
+      const float4* U4 = reinterpret_cast<const float4*>(RW + 2 * CL + k0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 gq = gl4[q];
+        const float4 u = basis ? make_float4(0.f, 0.f, 0.f, 0.f) : U4[q];
+        st[4 * q] = fmaf(st[4 * q], gq.x, u.x) + d2[4 * q];
+        st[4 * q + 1] = fmaf(st[4 * q + 1], gq.y, u.y) + d2[4 * q + 1];
+        st[4 * q + 2] = fmaf(st[4 * q + 2], gq.z, u.z) + d2[4 * q + 2];
+        st[4 * q + 3] = fmaf(st[4 * q + 3], gq.w, u.w) + d2[4 * q + 3];
+      }
+    }
+    __syncthreads();  // the stage, the operands and the accumulator are free again
+  }
+  if (ok) {
+    if (!basis) {
+      float* dst = (nseg == 1 ? rnn + (((size_t)slot * H + h) * KD + vrow) * KD
+                              : lbuf + (((size_t)gs * H + h) * KD + vrow) * KD) + k0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(dst)[q] = make_float4(st[4 * q], st[4 * q + 1], st[4 * q + 2], st[4 * q + 3]);
+    } else if (need_basis) {  // column vrow of the segment's transfer matrix
+      float* o = phi + ((size_t)gs * H + h) * (KD * KD) + (size_t)k0 * KD + vrow;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) o[k * KD] = st[k];
+    }
+  } else if (tid == 0) {
+    // leave no bulk copy in flight into this CTA's shared memory
+    for (int i = waited; i < issued; ++i) sc_mbar_wait(&full[i & 1], (i >> 1) & 1);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TS_TMEM_COLS));
+}
+
 // grid = (S, H, 4 row quarters), block = 256. Walks a multi-segment sequence's segments
 // in order: the true start of segment g + 1 is phi[g] applied to the true start of g
 // plus g's zero-start end state (segment 0's end state, scanned from the true state,
@@ -1042,6 +1413,9 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   if (dev < 64 && !attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(k_scan_phi, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)SCAN_SMEM);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_seg_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)TS_SMEM);
     if (e != cudaSuccess) {
       rwkv_set_error("chunk_scan: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       return RWKV_ERR_CUDA;
@@ -1050,12 +1424,23 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   }
   // plain launch: thousands of early-placed segment CTAs would crowd the SMs prep runs on
   rwkv_chain_begin();
-  const int n_phi = maxs * H;
-  if ((rc = rwkv_launch("scan_phi", k_scan_phi, dim3(n_phi + maxs * H * (KD / SCAN_ROWS)),
-                        dim3(SCAN_THREADS), SCAN_SMEM, st, cs.rec, cu, chunk_cu, cs.seg_cu, slots,
-                        rnn, ybuf, cs.yf32, cs.lbuf, cs.qt, cs.phi, S, H, C, M, maxc, n_slots,
-                        n_phi)))
-    return rc;
+  static const bool scan_tc = [] {
+    const char* e = std::getenv("RWKV_B200_SCAN_TC");
+    return !(e && e[0] == '0');
+  }();
+  if (scan_tc) {
+    if ((rc = rwkv_launch("seg_scan_tc", k_seg_scan_tc, dim3(maxs * H), dim3(TS_THREADS), TS_SMEM,
+                          st, cs.rec, cu, chunk_cu, cs.seg_cu, slots, rnn, ybuf, cs.yf32,
+                          cs.lbuf, cs.qt, cs.phi, S, H, C, M, maxc, n_slots)))
+      return rc;
+  } else {
+    const int n_phi = maxs * H;
+    if ((rc = rwkv_launch("scan_phi", k_scan_phi, dim3(n_phi + maxs * H * (KD / SCAN_ROWS)),
+                          dim3(SCAN_THREADS), SCAN_SMEM, st, cs.rec, cu, chunk_cu, cs.seg_cu,
+                          slots, rnn, ybuf, cs.yf32, cs.lbuf, cs.qt, cs.phi, S, H, C, M, maxc,
+                          n_slots, n_phi)))
+      return rc;
+  }
   if ((rc = rwkv_launch("seg_combine", k_seg_combine, dim3(S, H, 4), dim3(256), 0, st, cs.seg_cu,
                         slots, cs.lbuf, cs.phi, cs.sst, rnn)))
     return rc;
