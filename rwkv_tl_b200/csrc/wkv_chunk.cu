@@ -1424,10 +1424,16 @@ int launch_wkv_chunked(const __half* r, const __half* w, const __half* k, const 
   }
   // plain launch: thousands of early-placed segment CTAs would crowd the SMs prep runs on
   rwkv_chain_begin();
-  static const bool scan_tc = [] {
+  // The tensor-core scan's chunk step is a longer dependent chain (two MMA round trips per
+  // chunk) than the CUDA-core scan's, and wins once there are enough (segment, head) units
+  // to keep two per SM busy (measured on 0.4B: single sequences of T <= 256 favour the
+  // CUDA-core scan, T >= 512 and long varlen batches the tensor-core scan).
+  // RWKV_B200_SCAN_TC=0 / 1 forces either.
+  static const int scan_tc_env = [] {
     const char* e = std::getenv("RWKV_B200_SCAN_TC");
-    return !(e && e[0] == '0');
+    return e ? (e[0] == '0' ? 0 : 1) : -1;
   }();
+  const bool scan_tc = scan_tc_env >= 0 ? scan_tc_env == 1 : maxs * H >= 64;
   if (scan_tc) {
     if ((rc = rwkv_launch("seg_scan_tc", k_seg_scan_tc, dim3(maxs * H), dim3(TS_THREADS), TS_SMEM,
                           st, cs.rec, cu, chunk_cu, cs.seg_cu, slots, rnn, ybuf, cs.yf32,
