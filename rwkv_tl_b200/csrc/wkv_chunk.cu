@@ -1117,7 +1117,12 @@ __global__ void __launch_bounds__(TS_THREADS, 2) k_seg_scan_tc(
 // in order: the true start of segment g + 1 is phi[g] applied to the true start of g
 // plus g's zero-start end state (segment 0's end state, scanned from the true state,
 // is already the true start of segment 1). Start states go to sst for k_seg_fix; the final state
-// to rnn. Thread: key k = tid & 63, rows 4 (tid >> 6) .. +3 of the quarter.
+// to rnn. Thread: key k = tid & 63, rows 4 (tid >> 6) .. +3 of the quarter. The product is
+// bound by shared-memory wavefronts, so both operands are read 16 bytes at a time: a row
+// of Phi four columns per load, and the quarter's state stored transposed so that the four
+// rows a thread updates come in one broadcast load. Each sum still runs in j order.
+constexpr int CMB_PLD = KD + 4;  // Phi row stride: 8 lanes' 16-byte loads on distinct banks
+constexpr int CMB_SLD = 16 + 4;  // transposed state row stride (16 rows + pad), same reason
 __global__ void __launch_bounds__(256) k_seg_combine(const int* __restrict__ seg_cu,
                                                      const int* __restrict__ slots,
                                                      const float* __restrict__ lbuf,
@@ -1125,8 +1130,8 @@ __global__ void __launch_bounds__(256) k_seg_combine(const int* __restrict__ seg
                                                      float* __restrict__ sst,
                                                      float* __restrict__ rnn) {
   RWKV_GRID_DEP_ENTRY();
-  __shared__ float Ps[KD][KD + 1];   // Phi, padded: lanes walk rows k at a common column j
-  __shared__ float Sm[16][KD];       // the quarter's 16 state rows
+  __shared__ __align__(16) float Ps[KD * CMB_PLD];  // Phi[k][j] at k * CMB_PLD + j
+  __shared__ __align__(16) float St[KD * CMB_SLD];  // state row v, column j at j * CMB_SLD + v
   const int s = blockIdx.x, h = blockIdx.y, H = gridDim.y, q = blockIdx.z, tid = threadIdx.x;
   const int seg0 = seg_cu[s], nseg = seg_cu[s + 1] - seg0;
   if (nseg < 2) return;
@@ -1149,24 +1154,30 @@ __global__ void __launch_bounds__(256) k_seg_combine(const int* __restrict__ seg
   for (int g = 1; g < nseg; ++g) {
     const size_t so = seg_off(g);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      sst[so + rbase + (v0 + e) * KD + k] = st[e];
-      Sm[v0 + e][k] = st[e];
-    }
+    for (int e = 0; e < 4; ++e) sst[so + rbase + (v0 + e) * KD + k] = st[e];
+    *reinterpret_cast<float4*>(St + k * CMB_SLD + v0) = make_float4(st[0], st[1], st[2], st[3]);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int idx = tid + 256 * i;
-      Ps[idx / KD][idx % KD] = pp[i];
+      Ps[(idx / KD) * CMB_PLD + idx % KD] = pp[i];
     }
     float acc[4] = {pl[0], pl[1], pl[2], pl[3]};
     __syncthreads();
     if (g + 1 < nseg) fetch(g + 1);
     // start of segment g + 1 = Phi_g (start of g) + (g's zero-start end state)
-#pragma unroll 8
-    for (int j = 0; j < KD; ++j) {
-      const float p = Ps[k][j];
+    const float4* P4 = reinterpret_cast<const float4*>(Ps + k * CMB_PLD);
+#pragma unroll 4
+    for (int j4 = 0; j4 < KD / 4; ++j4) {
+      const float4 p4 = P4[j4];
+      const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] += p * Sm[v0 + e][j];
+      for (int jj = 0; jj < 4; ++jj) {
+        const float4 s4 = *reinterpret_cast<const float4*>(St + (4 * j4 + jj) * CMB_SLD + v0);
+        acc[0] += pj[jj] * s4.x;
+        acc[1] += pj[jj] * s4.y;
+        acc[2] += pj[jj] * s4.z;
+        acc[3] += pj[jj] * s4.w;
+      }
     }
 #pragma unroll
     for (int e = 0; e < 4; ++e) st[e] = acc[e];
