@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -161,6 +162,41 @@ size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)16 * M * C : 0; 
 
 // The chunk-parallel wkv pays off once sequences are long; one-token rows
 // (decode) use the fused per-token kernel. RWKV_B200_WKV=serial|chunked forces one.
+// Side stream for the r/k/v projections of small token batches (decode): those GEMMs
+// fill only part of the GPU (one 128 x 64 tile per CTA, one CTA per SM) and nothing but
+// the gate kernel reads their output, so they run beside the LoRA chain (down, reduce,
+// up) instead of before it. One non-blocking stream and two events per device, created
+// on first use; RWKV_B200_FORK=0 keeps everything on the caller's stream.
+struct ForkRes {
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  bool ok = false;
+};
+ForkRes* fork_res() {
+  static const bool on = [] {
+    const char* e = std::getenv("RWKV_B200_FORK");
+    return !(e && e[0] == '0');
+  }();
+  if (!on) return nullptr;
+  static ForkRes res[64];
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  ForkRes& r = res[dev];
+  if (!r.ok && !r.side) {
+    if (cudaStreamCreateWithFlags(&r.side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&r.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&r.join, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      r.side = reinterpret_cast<cudaStream_t>(1);  // do not retry; stay on one stream
+      return nullptr;
+    }
+    r.ok = true;
+  }
+  return r.ok ? &r : nullptr;
+}
+
 bool use_chunked_wkv(int M, int S) {
   const char* e = getenv("RWKV_B200_WKV");
   if (e && e[0] == 's') return false;
@@ -270,6 +306,8 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const int ns = state->n_slots;
   const __half* emb = (const __half*)model->emb;
   const bool chunked = use_chunked_wkv(M, S);
+  // r/k/v beside the LoRA chain only while both fit on the GPU at once (decode batches)
+  ForkRes* fk = M <= 512 ? fork_res() : nullptr;
   rwkv_chain_begin();
   // columns 32..63 of the rank buffer (the zero padding of rank v) must read as zero
   if (cudaMemsetAsync(w.ranks, 0, (size_t)M * RANKS_LD * sizeof(__half), st) != cudaSuccess)
@@ -297,12 +335,22 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
                          (const __half*)Lw.ln1_b, (const __half*)Lw.mix6, st_tx, b->row_seq,
                          b->cu_seqlens, b->slots, w.xmix, xl_t, M, C, pend, st));
     {
-      // r/k/v projections: xmix planes r=0, k=2, v=3
+      // r/k/v projections: xmix planes r=0, k=2, v=3 (no split-K at these sizes, so the
+      // side stream never touches the split-K scratch the LoRA-down uses)
       rwkv7_gemm_problem p[3] = {
           {w.xmix + 0 * MC, wrkv + 0 * CC, w.rkv + 0 * MC, nullptr, M, C, C, C, C, C},
           {w.xmix + 2 * MC, wrkv + 1 * CC, w.rkv + 1 * MC, nullptr, M, C, C, C, C, C},
           {w.xmix + 3 * MC, wrkv + 2 * CC, w.rkv + 2 * MC, nullptr, M, C, C, C, C, C}};
-      TRY(gemm_launch_ws(p, 3, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
+      if (fk) {
+        if (cudaEventRecord(fk->fork, st) != cudaSuccess ||
+            cudaStreamWaitEvent(fk->side, fk->fork, 0) != cudaSuccess)
+          return rwkv_check_launch("fork");
+        rwkv_chain_begin();  // plain launch on the side stream
+        TRY(gemm_launch_ws(p, 3, RWKV_EPI_STORE, nullptr, 0, fk->side));
+        if (cudaEventRecord(fk->join, fk->side) != cudaSuccess) return rwkv_check_launch("join");
+        // the LoRA-down keeps its programmatic edge to the row kernel
+      } else
+        TRY(gemm_launch_ws(p, 3, RWKV_EPI_STORE, w.splitk, w.splitk_floats, st));
     }
     {
       // LoRA down-projections into the rank buffer: v, tanh(w), a, sigmoid(g), activations
@@ -330,6 +378,10 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
           {w.ranks + 256, up + 256, lo + 3 * MC * esz, nullptr, M, C, 256, R, R, C}};
       TRY(gemm_launch_ws(p, 4, f32 ? RWKV_EPI_STORE_F32 : RWKV_EPI_STORE, w.splitk,
                          w.splitk_floats, st));
+    }
+    if (fk) {
+      if (cudaStreamWaitEvent(st, fk->join, 0) != cudaSuccess) return rwkv_check_launch("join");
+      rwkv_chain_begin();  // the gate kernel waits for the side stream in full
     }
     TRY(launch_gates_ew(sem, w.lora, w.rkv, (const __half*)Lw.w0, (const __half*)Lw.a0,
                         (const __half*)Lw.v0, (const __half*)Lw.k_k, (const __half*)Lw.k_a,
