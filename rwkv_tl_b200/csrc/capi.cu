@@ -155,7 +155,12 @@ struct Work {
   unsigned long long* argmax_keys;  // [n_logits] greedy-head keys (zero between calls)
   float* splitk;       // split-K partial tiles for small-M GEMMs
   size_t splitk_floats;
+  float* splitk_side;  // the same for the r/k/v GEMM on the side stream (decode batches)
 };
+
+// token batches of at most this many rows run r/k/v on a side stream (measured: no gain
+// for prefill-sized batches, whose GEMMs fill the GPU by themselves)
+constexpr int kForkMaxRows = 512;
 
 // split-K only pays for small token batches
 size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)16 * M * C : 0; }
@@ -173,11 +178,8 @@ struct ForkRes {
   bool ok = false;
 };
 ForkRes* fork_res() {
-  static const bool on = [] {
-    const char* e = std::getenv("RWKV_B200_FORK");
-    return !(e && e[0] == '0');
-  }();
-  if (!on) return nullptr;
+  const char* e = std::getenv("RWKV_B200_FORK");
+  if (e && e[0] == '0') return nullptr;
   static ForkRes res[64];
   static std::mutex mu;
   int dev = 0;
@@ -226,6 +228,9 @@ Work carve(void* base, size_t& total, int M, int S, int L, int C, int n_logits) 
   w.chunk_rec = c.take<float>(wkv_chunk_record_bytes(M, S, C / RWKV_HD) / sizeof(float));
   w.splitk_floats = splitk_floats(M, C);
   w.splitk = w.splitk_floats ? c.take<float>(w.splitk_floats) : nullptr;
+  // a region of its own, as large, so the side-stream r/k/v GEMM splits exactly as it
+  // would on the caller's stream (same K-slices, same sums)
+  w.splitk_side = M <= kForkMaxRows && w.splitk_floats ? c.take<float>(w.splitk_floats) : nullptr;
   total = c.off;
   return w;
 }
@@ -307,7 +312,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const __half* emb = (const __half*)model->emb;
   const bool chunked = use_chunked_wkv(M, S);
   // r/k/v beside the LoRA chain only while both fit on the GPU at once (decode batches)
-  ForkRes* fk = M <= 512 ? fork_res() : nullptr;
+  ForkRes* fk = M <= kForkMaxRows && w.splitk_side ? fork_res() : nullptr;
   rwkv_chain_begin();
   // columns 32..63 of the rank buffer (the zero padding of rank v) must read as zero
   if (cudaMemsetAsync(w.ranks, 0, (size_t)M * RANKS_LD * sizeof(__half), st) != cudaSuccess)
@@ -335,8 +340,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
                          (const __half*)Lw.ln1_b, (const __half*)Lw.mix6, st_tx, b->row_seq,
                          b->cu_seqlens, b->slots, w.xmix, xl_t, M, C, pend, st));
     {
-      // r/k/v projections: xmix planes r=0, k=2, v=3 (no split-K at these sizes, so the
-      // side stream never touches the split-K scratch the LoRA-down uses)
+      // r/k/v projections: xmix planes r=0, k=2, v=3
       rwkv7_gemm_problem p[3] = {
           {w.xmix + 0 * MC, wrkv + 0 * CC, w.rkv + 0 * MC, nullptr, M, C, C, C, C, C},
           {w.xmix + 2 * MC, wrkv + 1 * CC, w.rkv + 1 * MC, nullptr, M, C, C, C, C, C},
@@ -346,7 +350,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
             cudaStreamWaitEvent(fk->side, fk->fork, 0) != cudaSuccess)
           return rwkv_check_launch("fork");
         rwkv_chain_begin();  // plain launch on the side stream
-        TRY(gemm_launch_ws(p, 3, RWKV_EPI_STORE, nullptr, 0, fk->side));
+        TRY(gemm_launch_ws(p, 3, RWKV_EPI_STORE, w.splitk_side, w.splitk_floats, fk->side));
         if (cudaEventRecord(fk->join, fk->side) != cudaSuccess) return rwkv_check_launch("join");
         // the LoRA-down keeps its programmatic edge to the row kernel
       } else

@@ -407,3 +407,31 @@ def test_wide_and_narrow_row_layouts_are_bit_identical(monkeypatch):
         out[mode] = (bs.rnn.clone(), bs.tmix_x.clone(), bs.cmix_x.clone(), lg.clone())
     for a, b in zip(out["wide"], out["narrow"]):
         assert torch.equal(a, b)
+
+
+def test_side_stream_rkv_is_bit_identical(monkeypatch):
+    """Decode batches (<= 512 rows) run the r/k/v projections on a side stream beside the
+    LoRA chain; the same kernels compute the same values, so turning the side stream off
+    (RWKV_B200_FORK=0) changes no bit of the states or the logits, eager or replayed from
+    a CUDA graph."""
+    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 9)
+    g = make_rwkv7("cuda", backend="b200", use_graph=True)(m.w)
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("RWKV_B200_FORK", mode)
+        for B in (64, 256):
+            bs = BatchedState(m.L, m.C, B, device="cuda")
+            gen = torch.Generator(device="cuda").manual_seed(B)
+            bs.rnn.normal_(0.0, 0.1, generator=gen)
+            toks = torch.tensor(_tokens(B, 4096, 80 + B), device="cuda")
+            lg = m.decode_batch(toks, bs)
+            bs2 = BatchedState(m.L, m.C, B, device="cuda")
+            bs2.rnn.copy_(bs.rnn)
+            for _ in range(2):
+                lg2 = g.decode_batch(toks, bs2)
+            torch.cuda.synchronize()
+            out[(mode, B)] = (bs.rnn.clone(), bs.cmix_x.clone(), lg.clone(), lg2.clone())
+        g = make_rwkv7("cuda", backend="b200", use_graph=True)(m.w)  # fresh captures
+    for B in (64, 256):
+        for a, b in zip(out[("1", B)], out[("0", B)]):
+            assert torch.equal(a, b)
