@@ -171,13 +171,15 @@ size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)16 * M * C : 0; 
 // fill only part of the GPU (one 128 x 64 tile per CTA, one CTA per SM) and nothing but
 // the gate kernel reads their output, so they run beside the LoRA chain (down, reduce,
 // up) instead of before it. One non-blocking stream and two events per device, created
-// on first use; RWKV_B200_FORK=0 keeps everything on the caller's stream.
+// on the first such call that is not being captured into a CUDA graph (a call captured
+// before them runs on the caller's stream alone, with the same results);
+// RWKV_B200_FORK=0 keeps everything on the caller's stream.
 struct ForkRes {
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
   bool ok = false;
 };
-ForkRes* fork_res() {
+ForkRes* fork_res(cudaStream_t st) {
   const char* e = std::getenv("RWKV_B200_FORK");
   if (e && e[0] == '0') return nullptr;
   static ForkRes res[64];
@@ -187,6 +189,9 @@ ForkRes* fork_res() {
   std::lock_guard<std::mutex> lk(mu);
   ForkRes& r = res[dev];
   if (!r.ok && !r.side) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+      return nullptr;  // create nothing inside a capture
     if (cudaStreamCreateWithFlags(&r.side, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&r.fork, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&r.join, cudaEventDisableTiming) != cudaSuccess) {
@@ -312,7 +317,7 @@ extern "C" int rwkv7_forward(const rwkv7_model* model, const rwkv7_batch* b,
   const __half* emb = (const __half*)model->emb;
   const bool chunked = use_chunked_wkv(M, S);
   // r/k/v beside the LoRA chain only while both fit on the GPU at once (decode batches)
-  ForkRes* fk = M <= kForkMaxRows && w.splitk_side ? fork_res() : nullptr;
+  ForkRes* fk = M <= kForkMaxRows && w.splitk_side ? fork_res(st) : nullptr;
   rwkv_chain_begin();
   // columns 32..63 of the rank buffer (the zero padding of rank v) must read as zero
   if (cudaMemsetAsync(w.ranks, 0, (size_t)M * RANKS_LD * sizeof(__half), st) != cudaSuccess)
