@@ -435,3 +435,47 @@ def test_side_stream_rkv_is_bit_identical(monkeypatch):
     for B in (64, 256):
         for a, b in zip(out[("1", B)], out[("0", B)]):
             assert torch.equal(a, b)
+
+
+def test_first_call_under_capture_runs_on_one_stream():
+    """The side stream is never created inside a stream capture: a process whose very
+    first decode-batch call is captured into a CUDA graph gets a one-stream graph whose
+    replay equals the eager step (fresh process, so nothing was created before)."""
+    import subprocess
+    import sys
+    import textwrap
+
+    code = textwrap.dedent("""
+        import torch
+        from rwkv_tl_b200 import BatchedState
+        from rwkv_tl_b200.synth import ModelConfig
+        from tests.test_model_gpu import _pair, _tokens
+        m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 9)
+        B = 64
+        toks = torch.tensor(_tokens(B, 4096, 5), device="cuda")
+        a = BatchedState(m.L, m.C, B, device="cuda")
+        b = BatchedState(m.L, m.C, B, device="cuda")
+        a.rnn.normal_(0.0, 0.1, generator=torch.Generator(device="cuda").manual_seed(1))
+        b.rnn.copy_(a.rnn)
+        lg = torch.empty(B, 4096, dtype=torch.float16, device="cuda")
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+            m.decode_batch(toks, a, logits=lg)
+        a.rnn.copy_(b.rnn)
+        a.tmix_x.zero_(); a.cmix_x.zero_()
+        g.replay()
+        ref = m.decode_batch(toks, b)
+        torch.cuda.synchronize()
+        assert torch.equal(lg, ref) and torch.equal(a.rnn, b.rnn), "graph != eager"
+        print("OK")
+    """)
+    import os
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, PYTHONPATH=str(root))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
