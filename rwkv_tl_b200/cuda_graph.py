@@ -180,7 +180,17 @@ class CUDAGraph(RWKV7Model):
 
         A caller-provided ``out`` is captured as the graph's output (keyed by its
         address); without one the graph owns its id buffer and the caller gets a copy.
+
+        Serving loops that keep token ids on the host can pass ``tokens`` (int64) and
+        ``out`` as pinned CPU tensors: the graph then also holds the host -> device copy of
+        the ids and the device -> host copy of the next ids, so a step is one replay. The
+        call returns as soon as the step is queued; ``out`` holds the next ids once the
+        current stream has been synchronised.
         """
+        if (isinstance(tokens, Tensor) and not tokens.is_cuda and tokens.is_pinned()
+                and tokens.dtype == torch.int64 and out is not None and not out.is_cuda
+                and out.is_pinned() and out.dtype == torch.int64):
+            return self._decode_batch_greedy_host(tokens, state, slots, out)
         tok = self.model._tokens(tokens)
         B = tok.numel()
         key = ("decg", B, state.rnn.data_ptr(), None if slots is None else slots.data_ptr(),
@@ -203,6 +213,35 @@ class CUDAGraph(RWKV7Model):
         if out is not None:
             return out
         return e.logits.clone()
+
+    def _decode_batch_greedy_host(self, tokens: Tensor, state: BatchedState,
+                                  slots: Tensor | None, out: Tensor) -> Tensor:
+        """``decode_batch_greedy`` with pinned host token ids in and next ids out, the two
+        copies captured into the graph with the step (keyed by both host addresses)."""
+        B = tokens.numel()
+        key = ("decgh", B, state.rnn.data_ptr(), None if slots is None else slots.data_ptr(),
+               tokens.data_ptr(), out.data_ptr())
+        e = self._get(key)
+        if e is None and key not in self._failed:
+            buf = torch.zeros(B, dtype=torch.long, device=self.w.device)
+            ids = torch.empty(B, dtype=torch.long, device=self.w.device)
+
+            def run(st):
+                buf.copy_(tokens.reshape(-1), non_blocking=True)
+                self.model.decode_batch_greedy(buf, st, slots, ids)
+                out.reshape(-1).copy_(ids, non_blocking=True)
+
+            scratch = BatchedState(self.L, self.C, state.n_slots, device=self.w.device)
+            g = self._capture(key, run, scratch, state, f"decode_batch_greedy_host(B={B})")
+            if g is not None:
+                e = _Entry(g, buf, ids)
+                self._put(key, e)
+        if e is None:
+            ids = self.model.decode_batch_greedy(self.model._tokens(tokens), state, slots)
+            out.reshape(-1).copy_(ids, non_blocking=True)
+            return out
+        e.graph.replay()
+        return out
 
     def prefill_batch(self, seqs, state, slots=None):
         return self.model.prefill_batch(seqs, state, slots)

@@ -479,3 +479,26 @@ def test_first_call_under_capture_runs_on_one_stream():
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True,
                        text=True, timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_graphed_greedy_on_pinned_host_buffers():
+    """decode_batch_greedy with pinned host ids in and out (the copies captured into the
+    graph) gives the same next ids and states as the device-buffer call, step after step,
+    including when the host buffers' contents change between replays."""
+    m, _ = _pair(ModelConfig(n_layer=2, n_embd=768, vocab=4096), 11)
+    g = make_rwkv7("cuda", backend="b200", use_graph=True)(m.w)
+    B = 64
+    a = BatchedState(m.L, m.C, B, device="cuda")
+    b = BatchedState(m.L, m.C, B, device="cuda")
+    a.rnn.normal_(0.0, 0.1, generator=torch.Generator(device="cuda").manual_seed(3))
+    b.rnn.copy_(a.rnn)
+    host_tok = torch.tensor(_tokens(B, 4096, 12), dtype=torch.int64).pin_memory()
+    host_out = torch.empty(B, dtype=torch.int64).pin_memory()
+    dev_ids = torch.empty(B, dtype=torch.int64, device="cuda")
+    for step in range(4):
+        g.decode_batch_greedy(host_tok, a, out=host_out)
+        g.decode_batch_greedy(host_tok.cuda(), b, out=dev_ids)
+        torch.cuda.synchronize()
+        assert torch.equal(host_out, dev_ids.cpu()), step
+        host_tok.copy_(host_out)  # feed the step's ids back, as a serving loop does
+    assert torch.equal(a.rnn, b.rnn) and torch.equal(a.cmix_x, b.cmix_x)
