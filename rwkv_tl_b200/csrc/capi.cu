@@ -165,8 +165,6 @@ constexpr int kForkMaxRows = 512;
 // split-K only pays for small token batches
 size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)16 * M * C : 0; }
 
-// The chunk-parallel wkv pays off once sequences are long; one-token rows
-// (decode) use the fused per-token kernel. RWKV_B200_WKV=serial|chunked forces one.
 // Side stream for the r/k/v projections of small token batches (decode): those GEMMs
 // fill only part of the GPU (one 128 x 64 tile per CTA, one CTA per SM) and nothing but
 // the gate kernel reads their output, so they run beside the LoRA chain (down, reduce,
@@ -204,6 +202,8 @@ ForkRes* fork_res(cudaStream_t st) {
   return r.ok ? &r : nullptr;
 }
 
+// The chunk-parallel wkv pays off once sequences are long; one-token rows
+// (decode) use the fused per-token kernel. RWKV_B200_WKV=serial|chunked forces one.
 bool use_chunked_wkv(int M, int S) {
   const char* e = getenv("RWKV_B200_WKV");
   if (e && e[0] == 's') return false;
