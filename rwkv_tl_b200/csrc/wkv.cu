@@ -255,7 +255,7 @@ struct DecVecs {
 };
 
 #ifndef WKV_DEC_MINB
-#define WKV_DEC_MINB 6  // measured: 6 beats 5 by 1 % of the B=256 step; 8 spills and loses 4 %
+#define WKV_DEC_MINB 6  // measured: 6 beats 5 by 1 % of the B=256 step; 7 and 8 spill (7: 13 % slower per launch, 8: 4 % on the step)
 #endif
 template <int SEM>
 __global__ void __launch_bounds__(256, WKV_DEC_MINB) k_wkv_decode(
