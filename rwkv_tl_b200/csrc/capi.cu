@@ -9,7 +9,6 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
-#include <mutex>
 
 #include "common.cuh"
 
@@ -168,10 +167,11 @@ size_t splitk_floats(int M, int C) { return M <= 1024 ? (size_t)16 * M * C : 0; 
 // Side stream for the r/k/v projections of small token batches (decode): those GEMMs
 // fill only part of the GPU (one 128 x 64 tile per CTA, one CTA per SM) and nothing but
 // the gate kernel reads their output, so they run beside the LoRA chain (down, reduce,
-// up) instead of before it. One non-blocking stream and two events per device, created
-// on the first such call that is not being captured into a CUDA graph (a call captured
-// before them runs on the caller's stream alone, with the same results);
-// RWKV_B200_FORK=0 keeps everything on the caller's stream.
+// up) instead of before it. One non-blocking stream and two events per device and host
+// thread (calls from different threads never share an event, so their fork / join points
+// cannot cross), created on the thread's first such call that is not being captured into
+// a CUDA graph (a call captured before them runs on the caller's stream alone, with the
+// same results); RWKV_B200_FORK=0 keeps everything on the caller's stream.
 struct ForkRes {
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
@@ -180,11 +180,9 @@ struct ForkRes {
 ForkRes* fork_res(cudaStream_t st) {
   const char* e = std::getenv("RWKV_B200_FORK");
   if (e && e[0] == '0') return nullptr;
-  static ForkRes res[64];
-  static std::mutex mu;
+  static thread_local ForkRes res[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lk(mu);
   ForkRes& r = res[dev];
   if (!r.ok && !r.side) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
